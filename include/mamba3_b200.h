@@ -1,0 +1,147 @@
+/*
+ * mamba3_b200 — C ABI of the B200 (sm_100a) Mamba-3 chunked-SSD and decode-step kernels.
+ *
+ * These entry points replace the Triton dispatch of jreoka/mamba3:
+ *   m3_scan_fwd  replaces  mamba3/ops.py:253-505   (_fused_chunk_scan / _fused_chunk_scan_impl,
+ *                                                   i.e. the per-chunk _chunk_main_kernel +
+ *                                                   _chunk_state_kernel launches of
+ *                                                   mamba3/_triton.py:416-561)
+ *   m3_step_fwd  replaces  mamba3/ops.py:87-190    (fused_step -> mamba3/_triton.py:950-1151)
+ *
+ * Conventions
+ *   - Every tensor is passed as an m3_tensor: device pointer, element dtype and element strides
+ *     (not bytes). Shapes are given once in the argument struct. A NULL data pointer marks an
+ *     optional tensor as absent.
+ *   - `stream` is a cudaStream_t (passed as void*). Kernels are enqueued on it; nothing
+ *     synchronises, allocates or frees memory, so every call can be captured in a CUDA graph.
+ *   - Return value: 0 on success, otherwise an M3_ERR_* code; m3_last_error() then returns a
+ *     human-readable message (thread-local). Shape/dtype/stride checks happen before launch.
+ *   - Device-side waits are bounded; a wait that gives up sets a device error word that
+ *     m3_device_error() reads (synchronising the device).
+ */
+#ifndef MAMBA3_B200_H
+#define MAMBA3_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define M3_ABI_VERSION 1
+
+enum m3_dtype { M3_F32 = 0, M3_F16 = 1, M3_BF16 = 2 };
+
+enum m3_status {
+  M3_OK = 0,
+  M3_ERR_SHAPE = 1,       /* a shape is inconsistent or unsupported */
+  M3_ERR_DTYPE = 2,       /* an unsupported or inconsistent dtype */
+  M3_ERR_LAYOUT = 3,      /* a stride/alignment requirement is not met */
+  M3_ERR_ARGUMENT = 4,    /* missing required tensor / invalid flag */
+  M3_ERR_CUDA = 5,        /* a CUDA runtime error at launch */
+};
+
+typedef struct m3_tensor {
+  void* data;             /* device pointer, NULL = absent */
+  int32_t dtype;          /* enum m3_dtype */
+  int32_t ndim;           /* number of valid entries in stride[] */
+  int64_t stride[6];      /* element strides, outermost first */
+} m3_tensor;
+
+/*
+ * Chunked SSD forward over a whole sequence (prefill / forward).
+ * Semantics: mamba3/ops.py:544-822 (mamba3_scan), including the endpoint-cache continuation
+ * (ops.py:679-686), q/k head expansion + bias + rotation (ops.py:698-714) and the bidirectional
+ * reverse direction of mamba3/model.py:330-362 when `reverse` is set.
+ *
+ * Inputs (B=batch, L=length, G=groups, H=heads, R=rank, N=d_state, P=head_dim, S=num_angles):
+ *   q, k            [B,L,G,R,N]  activation dtype; rows are RMS-normalised in-kernel when
+ *                                q_norm_w/k_norm_w are given ([N], any float dtype)
+ *   q_bias, k_bias  [H,R,N]      optional, added after head expansion (model.py:211-212)
+ *   value, gate     [B,L,H,P]    activation dtype
+ *   adt, dt         [B,L,H]      float32 discretisation, or — when dt_bias is given — the raw
+ *                                decay/delta logits of the in_proj split (model.py:195-198):
+ *                                dt = softplus(delta + dt_bias), adt = min(-heavytail(a), -1e-4)*dt
+ *   trap            [B,L,H]      trapezoid logits (any float dtype)
+ *   phase           [B,L,H,S]    optional float32 precomputed phase, or
+ *   angles          [B,L,S]      optional raw angle logits: the phase is accumulated in-kernel
+ *                                with the 64-token blocked fmod scheme of model.py:215-256,
+ *                                starting from initial_phase [B,H,S] (float32, optional)
+ *   D               [H]
+ *   mimo_x/z/out    [H,R,P]      required iff R > 1
+ *   initial_state   [B,H,P,N]    float32, optional
+ *   initial_k       [B,H,R,N]    optional endpoint cache (rotated previous k)
+ *   initial_value   [B,H,P]      optional endpoint cache (previous value)
+ * Outputs:
+ *   y               [B,L,H,P]    activation dtype
+ *   final_state     [B,H,P,N]    float32
+ *   final_phase     [B,H,S]      float32, optional (phase at the last token)
+ *   final_k         [B,H,R,N]    activation dtype, optional (biased, rotated k of the last token)
+ */
+typedef struct m3_scan_args {
+  int32_t batch, length, groups, heads, rank, d_state, head_dim, num_angles;
+  int32_t reverse;        /* 1: scan tokens L-1..0 (bidirectional backward direction) */
+  int32_t mimo_rotation;  /* 1: rotate pairs (i, 2S+i) (MIMO layout); 0: adjacent pairs (2i, 2i+1) */
+  int32_t chunk_hint;     /* caller's chunk size (validated > 0; the kernel tiles internally) */
+  int32_t device;         /* CUDA device ordinal of every tensor and of `stream` (-1: current) */
+  float norm_eps;         /* RMS-norm epsilon for q_norm_w / k_norm_w */
+  int32_t reserved;
+  m3_tensor q, k, q_norm_w, k_norm_w, q_bias, k_bias;
+  m3_tensor value, gate;
+  m3_tensor adt, dt, trap, dt_bias;
+  m3_tensor phase, angles, initial_phase;
+  m3_tensor D, mimo_x, mimo_z, mimo_out;
+  m3_tensor initial_state, initial_k, initial_value;
+  m3_tensor y, final_state, final_phase, final_k;
+} m3_scan_args;
+
+/*
+ * One decode step (mamba3/ops.py:87-190 contract; math of mamba3/model.py:460-484 +
+ * mamba3/ops.py:825-879): advance the phase, rotate q/k, update the FP32 state with the
+ * exp-trapezoidal rule, y = sum_r mo_r * silu(z mz_r) * (S' q_r + D v_r).
+ *   q, k        [B,H,R,N]  activation dtype, unrotated (strides may be 0 along H)
+ *   q_bias/k_bias [H,R,N]  optional, added before rotation
+ *   value, gate [B,H,P]
+ *   adt, dt     [B,H]      float32;  trap [B,H] any float dtype
+ *   angle_rate  [B,S]      raw angle logits (shared across heads)
+ *   D [H]; mimo_x/z/out [H,R,P] iff R > 1
+ *   phase [B,H,S] f32, state [B,H,P,N] f32, prev_k [B,H,R,N], prev_value [B,H,P]  (the cache)
+ * Outputs: y [B,H,P]; out_phase [B,H,S] f32; out_state [B,H,P,N] f32 (may alias `state`
+ * exactly, for in-place decoding); out_k [B,H,R,N] (rotated k). out_phase/out_k must not
+ * alias phase/prev_k.
+ */
+typedef struct m3_step_args {
+  int32_t batch, heads, rank, d_state, head_dim, num_angles;
+  int32_t device;         /* CUDA device ordinal of every tensor and of `stream` (-1: current) */
+  int32_t reserved;
+  m3_tensor q, k, q_bias, k_bias, value, gate;
+  m3_tensor adt, dt, trap, angle_rate, D, mimo_x, mimo_z, mimo_out;
+  m3_tensor phase, state, prev_k, prev_value;
+  m3_tensor y, out_phase, out_state, out_k;
+} m3_step_args;
+
+/* Chunked SSD forward. Returns M3_OK or an M3_ERR_* code. */
+int m3_scan_fwd(const m3_scan_args* args, void* stream);
+
+/* Decode step. Returns M3_OK or an M3_ERR_* code. */
+int m3_step_fwd(const m3_step_args* args, void* stream);
+
+/* Message for the last non-zero status returned on this host thread. */
+const char* m3_last_error(void);
+
+/* ABI version (M3_ABI_VERSION). */
+int m3_abi_version(void);
+
+/* Synchronises the current device and returns the device error word (0 = no bounded wait
+ * ever gave up); `clear` resets it. Never called on a hot path. */
+int m3_device_error(int clear);
+
+/* Name of the scan kernel variant the last m3_scan_fwd on this thread launched
+ * ("umma" for the tcgen05 tensor-core kernel, "simt" for the FP32 CUDA-core kernel). */
+const char* m3_last_scan_kernel(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA3_B200_H */

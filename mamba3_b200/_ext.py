@@ -1,0 +1,174 @@
+"""ctypes binding of the C-ABI library ``_lib/libmamba3_b200.so`` (see ``include/mamba3_b200.h``).
+
+This module only marshals torch tensors into the plain-pointer argument structs and enqueues the
+kernels on the current torch stream. It never falls back to another implementation: a missing or
+unloadable library raises ``RuntimeError`` when a CUDA call needs it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmamba3_b200.so"
+
+M3_F32, M3_F16, M3_BF16 = 0, 1, 2
+_DTYPES = {torch.float32: M3_F32, torch.float16: M3_F16, torch.bfloat16: M3_BF16}
+ABI_VERSION = 1
+
+
+class M3Tensor(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("dtype", ctypes.c_int32),
+        ("ndim", ctypes.c_int32),
+        ("stride", ctypes.c_int64 * 6),
+    ]
+
+
+_SCAN_TENSORS = (
+    "q", "k", "q_norm_w", "k_norm_w", "q_bias", "k_bias",
+    "value", "gate",
+    "adt", "dt", "trap", "dt_bias",
+    "phase", "angles", "initial_phase",
+    "D", "mimo_x", "mimo_z", "mimo_out",
+    "initial_state", "initial_k", "initial_value",
+    "y", "final_state", "final_phase", "final_k",
+)
+
+_STEP_TENSORS = (
+    "q", "k", "q_bias", "k_bias", "value", "gate",
+    "adt", "dt", "trap", "angle_rate", "D", "mimo_x", "mimo_z", "mimo_out",
+    "phase", "state", "prev_k", "prev_value",
+    "y", "out_phase", "out_state", "out_k",
+)
+
+
+class ScanArgs(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int32) for name in (
+        "batch", "length", "groups", "heads", "rank", "d_state", "head_dim", "num_angles",
+        "reverse", "mimo_rotation", "chunk_hint", "device")] + [
+        ("norm_eps", ctypes.c_float), ("reserved", ctypes.c_int32)] + [
+        (name, M3Tensor) for name in _SCAN_TENSORS]
+
+
+class StepArgs(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int32) for name in (
+        "batch", "heads", "rank", "d_state", "head_dim", "num_angles", "device", "reserved")] + [
+        (name, M3Tensor) for name in _STEP_TENSORS]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def library_path() -> Path:
+    return _LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load the CUDA library once; raise RuntimeError if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not _LIB_PATH.exists():
+            raise RuntimeError(
+                f"mamba3_b200 CUDA library not built ({_LIB_PATH}); run `python -m mamba3_b200._build`")
+        lib = ctypes.CDLL(str(_LIB_PATH))
+        lib.m3_scan_fwd.argtypes = [ctypes.POINTER(ScanArgs), ctypes.c_void_p]
+        lib.m3_scan_fwd.restype = ctypes.c_int
+        lib.m3_step_fwd.argtypes = [ctypes.POINTER(StepArgs), ctypes.c_void_p]
+        lib.m3_step_fwd.restype = ctypes.c_int
+        lib.m3_last_error.argtypes = []
+        lib.m3_last_error.restype = ctypes.c_char_p
+        lib.m3_abi_version.argtypes = []
+        lib.m3_abi_version.restype = ctypes.c_int
+        lib.m3_device_error.argtypes = [ctypes.c_int]
+        lib.m3_device_error.restype = ctypes.c_int
+        lib.m3_last_scan_kernel.argtypes = []
+        lib.m3_last_scan_kernel.restype = ctypes.c_char_p
+        if lib.m3_abi_version() != ABI_VERSION:
+            raise RuntimeError("mamba3_b200 library ABI mismatch; rebuild it")
+        _lib = lib
+    return _lib
+
+
+def _desc(t: torch.Tensor | None) -> M3Tensor:
+    d = M3Tensor()
+    if t is None:
+        return d
+    if t.dtype not in _DTYPES:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    if t.dim() > 6:
+        raise ValueError("at most 6 dimensions")
+    d.data = t.data_ptr()
+    d.dtype = _DTYPES[t.dtype]
+    d.ndim = t.dim()
+    for i, s in enumerate(t.stride()):
+        d.stride[i] = s
+    return d
+
+
+def _cuda_device(tensors: dict) -> torch.device:
+    device = tensors["value"].device
+    for name, t in tensors.items():
+        if t is not None and t.device != device:
+            raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if device.type != "cuda":
+        raise ValueError(f"the mamba3_b200 kernels need CUDA tensors, got {device}")
+    return device
+
+
+def _check(rc: int, lib) -> None:
+    if rc != 0:
+        msg = lib.m3_last_error().decode()
+        raise RuntimeError(f"mamba3_b200 kernel error {rc}: {msg}")
+
+
+@torch.compiler.disable
+def scan_forward(*, sizes: dict, tensors: dict, reverse: bool = False, mimo_rotation: bool = False,
+                 chunk_hint: int = 64, norm_eps: float = 1e-5) -> None:
+    """Enqueue ``m3_scan_fwd`` on the current stream of the tensors' device."""
+    lib = load()
+    args = ScanArgs()
+    for key, val in sizes.items():
+        setattr(args, key, int(val))
+    args.reverse = int(reverse)
+    args.mimo_rotation = int(mimo_rotation)
+    args.chunk_hint = int(chunk_hint)
+    args.norm_eps = float(norm_eps)
+    device = _cuda_device(tensors)
+    args.device = device.index if device.index is not None else torch.cuda.current_device()
+    for name in _SCAN_TENSORS:
+        setattr(args, name, _desc(tensors.get(name)))
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _check(lib.m3_scan_fwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
+
+
+@torch.compiler.disable
+def step_forward(*, sizes: dict, tensors: dict) -> None:
+    """Enqueue ``m3_step_fwd`` on the current stream of the tensors' device."""
+    lib = load()
+    args = StepArgs()
+    for key, val in sizes.items():
+        setattr(args, key, int(val))
+    device = _cuda_device(tensors)
+    args.device = device.index if device.index is not None else torch.cuda.current_device()
+    for name in _STEP_TENSORS:
+        setattr(args, name, _desc(tensors.get(name)))
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _check(lib.m3_step_fwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
+
+
+def last_scan_kernel() -> str:
+    return load().m3_last_scan_kernel().decode()
+
+
+def device_error(clear: bool = True) -> int:
+    return load().m3_device_error(int(clear))

@@ -1,0 +1,518 @@
+"""``Mamba3`` module stack with the B200 kernels on the inference path.
+
+Same public API, constructor, parameter names/shapes/initialisation order (hence identical
+``state_dict`` and identical seeded initialisation) and cache layout as ``mamba3/model.py`` of
+jreoka/mamba3. What changes is the CUDA inference path of each mixer:
+
+* forward / prefill: one ``in_proj`` GEMM, then ONE kernel launch per mixer (per direction) that
+  reads the raw projection columns directly — B/C RMS-norm, head bias, softplus/heavy-tail
+  discretisation, the 64-token blocked phase and the rotation all happen inside the chunked-SSD
+  kernel — then the ``out_proj`` GEMM. The reference instead materialises the head-expanded,
+  rotated q/k and runs a Python loop of two launches per chunk plus an L/64-iteration phase loop.
+* step: one decode kernel per mixer; under :meth:`Mamba3.cuda_graph` it updates the FP32 state in
+  place, so a graph replay streams the state through HBM once (read + write).
+
+Training (autograd) and CPU tensors run the PyTorch formulation in :mod:`mamba3_b200.ops`.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+from torch import nn
+from torch.nn import functional as F
+
+from . import _ext, ops
+from .ops import _kernel_eligible, _step_device, fused_step, heavy_tail_activation, mamba3_scan, mamba3_step, rotate_qk
+
+_EXPANSION = 2
+_CANONICAL_HEAD_DIM = 64
+_ROPE_FRACTION = 0.5
+_A_FLOOR = 1e-4
+_PHASE_CHUNK = 64
+
+_LayerCache = tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]
+
+
+def _default_chunk_sizes(mimo_rank: int) -> tuple[int, int]:
+    """(training, inference) chunk sizes of mamba3/model.py:26-37."""
+    training = 512 if mimo_rank == 1 else max(8, 64 // mimo_rank)
+    inference = 256 if mimo_rank == 1 else max(16, 128 // mimo_rank)
+    return training, inference
+
+
+class _RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float = 1e-5) -> None:
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.rms_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.eps).to(x.dtype)
+
+
+class _Mamba3Mixer(nn.Module):
+    """Mamba-3 SISO/MIMO mixer (mamba3/model.py:58-484); bidirectional when ``causal=False``."""
+
+    def __init__(self, d_model: int, d_state: int, mimo_rank: int, causal: bool = True) -> None:
+        super().__init__()
+        self.d_model = d_model
+        self.d_state = d_state
+        self.mimo_rank = mimo_rank
+        self.causal = causal
+        self.d_inner = _EXPANSION * d_model
+        self.headdim = math.gcd(self.d_inner, _CANONICAL_HEAD_DIM)
+        self.nheads = self.d_inner // self.headdim
+        self.ngroups = 1
+        self.num_angles = int(d_state * _ROPE_FRACTION) // 2
+        train_chunk, inference_chunk = _default_chunk_sizes(mimo_rank)
+        override = os.getenv("MAMBA3_CHUNK_SIZE")
+        if override:
+            try:
+                value = int(override)
+            except ValueError as error:
+                raise ValueError("MAMBA3_CHUNK_SIZE must be a positive integer") from error
+            if value <= 0:
+                raise ValueError("MAMBA3_CHUNK_SIZE must be a positive integer")
+            train_chunk = inference_chunk = value
+        self.chunk_size = train_chunk
+        self.inference_chunk_size = inference_chunk
+        # Set by _CudaGraphDecoder while it captures: the step kernel then writes the state into
+        # the cache tensor it was given (the decoder owns that cache).
+        self._state_in_place = False
+
+        width = 2 * self.d_inner + 2 * d_state * self.ngroups * mimo_rank + 3 * self.nheads + self.num_angles
+        # Parameter creation order matches the reference so seeded initialisation is identical.
+        self.in_proj = nn.Linear(d_model, width, bias=False)
+        self.B_norm = _RMSNorm(d_state)
+        self.C_norm = _RMSNorm(d_state)
+        self.B_bias = nn.Parameter(torch.ones(self.nheads, mimo_rank, d_state))
+        self.C_bias = nn.Parameter(torch.ones(self.nheads, mimo_rank, d_state))
+        dt = torch.exp(torch.rand(self.nheads) * (math.log(0.1) - math.log(0.001)) + math.log(0.001)).clamp_min(1e-4)
+        self.dt_bias = nn.Parameter(dt + torch.log(-torch.expm1(-dt)))
+        self.dt_bias._no_weight_decay = True
+        self.D = nn.Parameter(torch.ones(self.nheads))
+        self.D._no_weight_decay = True
+        if mimo_rank > 1:
+            self.mimo_x = nn.Parameter(torch.full((self.nheads, mimo_rank, self.headdim), 1.0 / mimo_rank))
+            self.mimo_z = nn.Parameter(torch.ones(self.nheads, mimo_rank, self.headdim))
+            self.mimo_out = nn.Parameter(torch.full((self.nheads, mimo_rank, self.headdim), 1.0 / mimo_rank))
+        else:
+            self.register_parameter("mimo_x", None)
+            self.register_parameter("mimo_z", None)
+            self.register_parameter("mimo_out", None)
+        self.out_proj = nn.Linear(self.d_inner, d_model, bias=False)
+        if causal:
+            self.register_parameter("direction_logit", None)
+        else:
+            self.direction_logit = nn.Parameter(torch.zeros(d_model))
+
+    # ---- projection -------------------------------------------------------------------------
+
+    def _split_projection(self, projected: torch.Tensor) -> tuple[torch.Tensor, ...]:
+        """Views of [z, x, B, C, delta, decay, trap, angles] (mamba3/model.py:147-163)."""
+        bc = self.d_state * self.ngroups * self.mimo_rank
+        return torch.split(projected, (self.d_inner, self.d_inner, bc, bc, self.nheads, self.nheads, self.nheads,
+                                       self.num_angles), dim=-1)
+
+    def _views(self, projected: torch.Tensor):
+        batch, length, _ = projected.shape
+        z, x, B, C, delta, decay, trap, angles = self._split_projection(projected)
+        z = z.unflatten(-1, (self.nheads, self.headdim))
+        x = x.unflatten(-1, (self.nheads, self.headdim))
+        # [B, L, R, G, N] -> [B, L, G, R, N]
+        B = B.reshape(batch, length, self.mimo_rank, self.ngroups, self.d_state).transpose(2, 3)
+        C = C.reshape(batch, length, self.mimo_rank, self.ngroups, self.d_state).transpose(2, 3)
+        return z, x, B, C, delta, decay, trap, angles
+
+    def _project(self, hidden_states: torch.Tensor):
+        """Projection + B/C norm + discretisation (mamba3/model.py:165-199)."""
+        z, x, B, C, delta, decay, trap, angles = self._views(self.in_proj(hidden_states))
+        k = self.B_norm(B)
+        q = self.C_norm(C)
+        dt = F.softplus(delta.float() + self.dt_bias.float())
+        A = (-heavy_tail_activation(decay.float())).clamp(max=-_A_FLOOR)
+        return q, k, x, z, A * dt, dt, trap, angles
+
+    def _expand_qk(self, q: torch.Tensor, k: torch.Tensor):
+        """Head expansion + bias (mamba3/model.py:201-213)."""
+        if q.shape[2] == 1:
+            q = q.expand(-1, -1, self.nheads, -1, -1)
+            k = k.expand(-1, -1, self.nheads, -1, -1)
+        elif q.shape[2] != self.nheads:
+            q = q.repeat_interleave(self.nheads // q.shape[2], dim=2)
+            k = k.repeat_interleave(self.nheads // k.shape[2], dim=2)
+        return q + self.C_bias[None, None].to(q.dtype), k + self.B_bias[None, None].to(k.dtype)
+
+    def _phase(self, angles: torch.Tensor, dt: torch.Tensor, initial_phase: torch.Tensor | None) -> torch.Tensor:
+        """Blocked FP32 phase accumulation (mamba3/model.py:215-256).
+
+        Increments fmod(pi tanh(angle) dt, 2pi) are summed from the start of each 64-token block;
+        the block offset is carried with an fmod at every block end, so partial sums never grow
+        beyond one block (keeps FP32 phase exact at long context).
+        """
+        inc = torch.fmod(math.pi * torch.tanh(angles.float()).unsqueeze(2) * dt.unsqueeze(-1), 2.0 * math.pi)
+        batch, length, heads, count = inc.shape
+        pad = (-length) % _PHASE_CHUNK
+        if pad:
+            inc = F.pad(inc, (0, 0, 0, 0, 0, pad))
+        blocks = inc.shape[1] // _PHASE_CHUNK
+        local = torch.cumsum(inc.reshape(batch, blocks, _PHASE_CHUNK, heads, count), dim=2)
+        offset = torch.zeros_like(local[:, 0, 0]) if initial_phase is None else initial_phase
+        starts = []
+        for index in range(blocks):
+            starts.append(offset)
+            offset = torch.fmod(offset + local[:, index, -1], 2.0 * math.pi)
+        phase = torch.fmod(local + torch.stack(starts, dim=1).unsqueeze(2), 2.0 * math.pi)
+        return phase.reshape(batch, -1, heads, count)[:, :length]
+
+    def _phase_and_rotate(self, q, k, angles, dt, initial_phase):
+        phase = self._phase(angles, dt, initial_phase)
+        q, k = rotate_qk(q, k, phase, mimo=self.mimo_rank > 1)
+        return q, k, phase
+
+    # ---- forward ----------------------------------------------------------------------------
+
+    def _scan_fused(self, projected: torch.Tensor, cache: _LayerCache | None, *, reverse: bool, want_cache: bool):
+        """One kernel launch for the whole SSD of this mixer (one direction), from raw projections."""
+        z, x, B, C, delta, decay, trap, angles = self._views(projected)
+        batch, length = projected.shape[:2]
+        act = projected.dtype
+        y = torch.empty(batch, length, self.nheads, self.headdim, device=projected.device, dtype=act)
+        state = torch.empty(batch, self.nheads, self.headdim, self.d_state, device=projected.device,
+                            dtype=torch.float32)
+        final_phase = final_k = None
+        if want_cache:
+            final_phase = torch.empty(batch, self.nheads, self.num_angles, device=projected.device,
+                                      dtype=torch.float32)
+            final_k = torch.empty(batch, self.nheads, self.mimo_rank, self.d_state, device=projected.device, dtype=act)
+        tensors = dict(q=C, k=B, q_norm_w=self.C_norm.weight, k_norm_w=self.B_norm.weight, q_bias=self.C_bias,
+                       k_bias=self.B_bias, value=x, gate=z, adt=decay, dt=delta, trap=trap, dt_bias=self.dt_bias,
+                       angles=angles, D=self.D, mimo_x=self.mimo_x, mimo_z=self.mimo_z, mimo_out=self.mimo_out,
+                       y=y, final_state=state, final_phase=final_phase, final_k=final_k)
+        if cache is not None:
+            tensors.update(initial_phase=cache[0], initial_state=cache[1], initial_k=cache[2].to(act),
+                           initial_value=cache[3].to(act))
+        sizes = dict(batch=batch, length=length, groups=self.ngroups, heads=self.nheads, rank=self.mimo_rank,
+                     d_state=self.d_state, head_dim=self.headdim, num_angles=self.num_angles)
+        _ext.scan_forward(sizes=sizes, tensors=tensors, reverse=reverse, mimo_rotation=self.mimo_rank > 1,
+                          chunk_hint=self.inference_chunk_size, norm_eps=self.C_norm.eps)
+        ops.LAST_SCAN_DISPATCH = True
+        return y, state, final_phase, final_k, x
+
+    def _use_kernels(self, hidden_states: torch.Tensor) -> bool:
+        return _kernel_eligible(hidden_states, *self.parameters())
+
+    def forward(self, hidden_states: torch.Tensor, cache: _LayerCache | None = None, *, return_cache: bool = False):
+        if not self.causal and (cache is not None or return_cache):
+            raise ValueError("bidirectional Mamba3 does not support caches; prefill and step require causal=True")
+        if self._use_kernels(hidden_states):
+            return self._forward_kernels(hidden_states, cache, return_cache)
+        return self._forward_torch(hidden_states, cache, return_cache)
+
+    def _forward_kernels(self, hidden_states, cache, return_cache):
+        projected = self.in_proj(hidden_states)
+        mixed, state, phase, k_last, x = self._scan_fused(projected, cache, reverse=False, want_cache=return_cache)
+        output = self.out_proj(mixed.flatten(-2))
+        if self.causal:
+            if not return_cache:
+                return output
+            return output, (phase, state, k_last, x[:, -1].clone())
+        # Backward direction: same projections read back to front, phase restarted at the end.
+        mixed_r, _, _, _, _ = self._scan_fused(projected, None, reverse=True, want_cache=False)
+        backward = self.out_proj(mixed_r.flatten(-2))
+        blend = torch.sigmoid(self.direction_logit).to(output.dtype)
+        return output * blend + backward * (1.0 - blend)
+
+    def _scan_torch_direction(self, hidden_states, cache):
+        q, k, x, z, adt, dt, trap, angles = self._project(hidden_states)
+        phase = self._phase(angles, dt, cache[0] if cache is not None else None)
+        chunk = self.chunk_size if self.training and torch.is_grad_enabled() else self.inference_chunk_size
+        mixed, state = mamba3_scan(
+            q, k, x, z, adt, dt, trap, self.D, mimo_x=self.mimo_x, mimo_z=self.mimo_z, mimo_out=self.mimo_out,
+            chunk_size=chunk, initial_state=cache[1] if cache is not None else None,
+            initial_k=cache[2] if cache is not None else None, initial_value=cache[3] if cache is not None else None,
+            phase=phase, mimo_rotation=self.mimo_rank > 1, q_bias=self.C_bias, k_bias=self.B_bias)
+        return mixed, state, phase, q, k, x
+
+    def _forward_torch(self, hidden_states, cache, return_cache):
+        mixed, state, phase, q, k, x = self._scan_torch_direction(hidden_states, cache)
+        output = self.out_proj(mixed.flatten(-2))
+        if self.causal:
+            if not return_cache:
+                return output
+            q_last, k_last = self._expand_qk(q[:, -1:], k[:, -1:])
+            _, k_last = rotate_qk(q_last, k_last, phase[:, -1:], mimo=self.mimo_rank > 1)
+            return output, (phase[:, -1].clone(), state, k_last[:, 0].clone(), x[:, -1].clone())
+        mixed_r, _, _, _, _, _ = self._scan_torch_direction(torch.flip(hidden_states, dims=(1,)), None)
+        backward = self.out_proj(torch.flip(mixed_r, dims=(1,)).flatten(-2))
+        blend = torch.sigmoid(self.direction_logit).to(output.dtype)
+        return output * blend + backward * (1.0 - blend)
+
+    # ---- decode -----------------------------------------------------------------------------
+
+    def allocate_cache(self, batch_size: int, *, device: torch.device, dtype: torch.dtype) -> _LayerCache:
+        """Zero cache (phase, FP32 state, rotated k, value) of mamba3/model.py:364-402."""
+        return (
+            torch.zeros(batch_size, self.nheads, self.num_angles, device=device, dtype=torch.float32),
+            torch.zeros(batch_size, self.nheads, self.headdim, self.d_state, device=device, dtype=torch.float32),
+            torch.zeros(batch_size, self.nheads, self.mimo_rank, self.d_state, device=device, dtype=dtype),
+            torch.zeros(batch_size, self.nheads, self.headdim, device=device, dtype=dtype),
+        )
+
+    def _validate_cache(self, cache: _LayerCache, batch_size: int) -> None:
+        if len(cache) != 4:
+            raise ValueError("a Mamba-3 layer cache must contain four tensors")
+        expected = (
+            (batch_size, self.nheads, self.num_angles),
+            (batch_size, self.nheads, self.headdim, self.d_state),
+            (batch_size, self.nheads, self.mimo_rank, self.d_state),
+            (batch_size, self.nheads, self.headdim),
+        )
+        actual = tuple(tuple(t.shape) for t in cache)
+        if actual != expected:
+            raise ValueError(f"expected cache shapes {expected}, got {actual}")
+        if cache[0].dtype != torch.float32 or cache[1].dtype != torch.float32:
+            raise ValueError("phase and SSM cache tensors must be float32")
+        device = self.in_proj.weight.device
+        if any(t.device != device for t in cache):
+            raise ValueError(f"cache tensors must be on {device}")
+
+    def step(self, hidden_states: torch.Tensor, cache: _LayerCache | None):
+        if hidden_states.ndim != 3 or hidden_states.shape[1:] != (1, self.d_model):
+            raise ValueError(f"expected [batch, 1, {self.d_model}], got {tuple(hidden_states.shape)}")
+        q, k, x, z, adt, dt, trap, angles = self._project(hidden_states)
+        if cache is None:
+            cache = self.allocate_cache(hidden_states.shape[0], device=hidden_states.device, dtype=x.dtype)
+        else:
+            self._validate_cache(cache, hidden_states.shape[0])
+        if self._use_kernels(hidden_states) and cache[2].dtype == q.dtype and cache[3].dtype == x.dtype:
+            # Bias and rotation happen in the kernel; q/k stay unexpanded views (stride 0 over heads).
+            heads = self.nheads
+            qh = q[:, 0].expand(-1, heads, -1, -1) if q.shape[2] == 1 else q[:, 0].repeat_interleave(
+                heads // q.shape[2], dim=1)
+            kh = k[:, 0].expand(-1, heads, -1, -1) if k.shape[2] == 1 else k[:, 0].repeat_interleave(
+                heads // k.shape[2], dim=1)
+            mixed, next_cache = _step_device(
+                qh, kh, x[:, 0], z[:, 0], adt[:, 0], dt[:, 0], trap[:, 0], angles[:, 0], self.D, cache,
+                mimo_x=self.mimo_x, mimo_z=self.mimo_z, mimo_out=self.mimo_out, q_bias=self.C_bias,
+                k_bias=self.B_bias, out_state=cache[1] if self._state_in_place else None)
+            return self.out_proj(mixed.flatten(-2)).unsqueeze(1), next_cache
+        q, k = self._expand_qk(q, k)
+        fused = fused_step(q[:, 0], k[:, 0], x[:, 0], z[:, 0], adt[:, 0], dt[:, 0], trap[:, 0], angles[:, 0], self.D,
+                           cache, mimo_x=self.mimo_x, mimo_z=self.mimo_z, mimo_out=self.mimo_out)
+        if fused is not None:
+            mixed, next_cache = fused
+            return self.out_proj(mixed.flatten(-2)).unsqueeze(1), next_cache
+        increment = torch.fmod(math.pi * torch.tanh(angles[:, 0].float()).unsqueeze(1) * dt[:, 0].unsqueeze(-1),
+                               2.0 * math.pi)
+        phase = torch.fmod(cache[0] + increment, 2.0 * math.pi)
+        q, k = rotate_qk(q, k, phase.unsqueeze(1), mimo=self.mimo_rank > 1)
+        mixed, next_cache = mamba3_step(q[:, 0], k[:, 0], x[:, 0], z[:, 0], adt[:, 0], dt[:, 0], trap[:, 0], self.D,
+                                        (phase, cache[1], cache[2], cache[3]), mimo_x=self.mimo_x,
+                                        mimo_z=self.mimo_z, mimo_out=self.mimo_out)
+        return self.out_proj(mixed.flatten(-2)).unsqueeze(1), next_cache
+
+
+class _Mamba3Block(nn.Module):
+    """RMSNorm -> mixer -> residual (mamba3/model.py:487-520)."""
+
+    def __init__(self, d_model: int, d_state: int, mimo_rank: int, causal: bool = True) -> None:
+        super().__init__()
+        self.norm = _RMSNorm(d_model)
+        self.mixer = _Mamba3Mixer(d_model, d_state, mimo_rank, causal=causal)
+
+    def forward(self, hidden_states, cache=None, *, return_cache: bool = False):
+        mixed = self.mixer(self.norm(hidden_states), cache=cache, return_cache=return_cache)
+        if return_cache:
+            output, next_cache = mixed
+            return hidden_states + output, next_cache
+        return hidden_states + mixed
+
+    def step(self, hidden_states, cache):
+        output, next_cache = self.mixer.step(self.norm(hidden_states), cache)
+        return hidden_states + output, next_cache
+
+
+class Mamba3(nn.Module):
+    """A shape-preserving stack of canonical Mamba-3 mixers (mamba3/model.py:523-688).
+
+    ``Mamba3(d_model, d_state=128, depth=4, mimo_rank=1, causal=True)``; inputs and outputs are
+    ``[batch, length, d_model]``. ``mimo_rank=4`` selects MIMO; ``causal=False`` the
+    bidirectional encoder variant.
+    """
+
+    def __init__(self, d_model: int, d_state: int = 128, depth: int = 4, mimo_rank: int = 1,
+                 causal: bool = True) -> None:
+        super().__init__()
+        if d_model <= 0:
+            raise ValueError("d_model must be positive")
+        if d_state < 4:
+            raise ValueError("d_state must be at least 4")
+        if mimo_rank > 1 and d_state % 4 != 0:
+            raise ValueError("MIMO requires d_state divisible by 4")
+        if depth <= 0:
+            raise ValueError("depth must be positive")
+        if mimo_rank <= 0:
+            raise ValueError("mimo_rank must be positive")
+        self.d_model = d_model
+        self.d_state = d_state
+        self.depth = depth
+        self.mimo_rank = mimo_rank
+        self.causal = causal
+        self.layers = nn.ModuleList(_Mamba3Block(d_model, d_state, mimo_rank, causal=causal) for _ in range(depth))
+        self.norm_f = _RMSNorm(d_model)
+        with torch.no_grad():
+            for layer in self.layers:
+                layer.mixer.out_proj.weight.div_(math.sqrt(depth))
+
+    def _validate_input(self, x: torch.Tensor, *, single_token: bool = False) -> None:
+        if x.ndim != 3 or x.shape[-1] != self.d_model:
+            raise ValueError(f"expected [batch, length, {self.d_model}], got {tuple(x.shape)}")
+        if single_token and x.shape[1:] != (1, self.d_model):
+            raise ValueError(f"expected [batch, 1, {self.d_model}], got {tuple(x.shape)}")
+
+    def _empty_output(self, x: torch.Tensor) -> torch.Tensor:
+        # Keeps every parameter in the autograd graph for empty inputs (mamba3/model.py:581-583).
+        tie = sum(p.sum() * 0.0 for p in self.parameters())
+        return x + tie.to(x.dtype)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        self._validate_input(x)
+        if x.shape[0] == 0 or x.shape[1] == 0:
+            return self._empty_output(x)
+        for layer in self.layers:
+            x = layer(x)
+        return self.norm_f(x)
+
+    def prefill(self, x: torch.Tensor):
+        """Process a causal prefix and return the constant-size decode cache."""
+        if not self.causal:
+            raise ValueError("prefill requires causal=True")
+        self._validate_input(x)
+        if x.shape[0] == 0 or x.shape[1] == 0:
+            raise ValueError("prefill requires a non-empty batch and sequence")
+        caches = []
+        for layer in self.layers:
+            x, layer_cache = layer(x, return_cache=True)
+            caches.append(layer_cache)
+        return self.norm_f(x), caches
+
+    def step(self, x: torch.Tensor, cache=None):
+        """Process one token while carrying Mamba-3's four recurrent states."""
+        if not self.causal:
+            raise ValueError("step requires causal=True")
+        self._validate_input(x, single_token=True)
+        if cache is None:
+            layer_caches = [None] * len(self.layers)
+        else:
+            if len(cache) != len(self.layers):
+                raise ValueError(f"expected cache for {len(self.layers)} layers")
+            layer_caches = list(cache)
+        new_cache = []
+        for layer, layer_cache in zip(self.layers, layer_caches):
+            x, updated = layer.step(x, layer_cache)
+            new_cache.append(updated)
+        return self.norm_f(x), new_cache
+
+    def set_chunk_sizes(self, *, training: int | None = None, inference: int | None = None) -> Mamba3:
+        """Override scan chunk sizes without rebuilding the model (mamba3/model.py:632-654)."""
+        if training is not None and training <= 0:
+            raise ValueError("training chunk size must be positive")
+        if inference is not None and inference <= 0:
+            raise ValueError("inference chunk size must be positive")
+        for layer in self.layers:
+            if training is not None:
+                layer.mixer.chunk_size = training
+            if inference is not None:
+                layer.mixer.inference_chunk_size = inference
+        return self
+
+    def compile_layers(self, **kwargs) -> Mamba3:
+        """torch.compile each block separately (mamba3/model.py:656-668)."""
+        for layer in self.layers:
+            layer.forward = torch.compile(layer.forward, **kwargs)
+        return self
+
+    def cuda_graph(self, batch_size: int = 1) -> _CudaGraphDecoder:
+        """Capture the complete stateful decode step in a CUDA graph."""
+        return _CudaGraphDecoder(self, batch_size)
+
+    def compile(self, **kwargs) -> Mamba3:
+        """Replace ``forward`` with a ``torch.compile``-wrapped version (mamba3/model.py:675-688)."""
+        self.forward = torch.compile(self.forward, **kwargs)
+        return self
+
+
+class _CudaGraphDecoder:
+    """Replays a captured ``Mamba3.step`` for a fixed batch (mamba3/model.py:691-774).
+
+    The decoder owns its cache, so the captured step kernels update the FP32 state in place; only
+    the small phase / k / value caches are copied back after each step.
+    """
+
+    def __init__(self, model: Mamba3, batch_size: int) -> None:
+        if batch_size <= 0:
+            raise ValueError("batch_size must be positive")
+        parameter = next(model.parameters())
+        if parameter.device.type != "cuda":
+            raise ValueError("cuda_graph requires a CUDA model")
+        if model.training:
+            raise ValueError("cuda_graph requires model.eval()")
+        self.model = model
+        self.parameters = tuple(model.parameters())
+        self.parameter_signature = self._parameter_signature()
+        device = parameter.device
+        self.input = torch.zeros(batch_size, 1, model.d_model, device=device, dtype=parameter.dtype)
+        self.cache = [layer.mixer.allocate_cache(batch_size, device=device, dtype=parameter.dtype)
+                      for layer in model.layers]
+        mixers = [layer.mixer for layer in model.layers]
+        try:
+            for mixer in mixers:
+                mixer._state_in_place = True
+            with torch.cuda.device(device):
+                warm = torch.cuda.Stream(device=device)
+                warm.wait_stream(torch.cuda.current_stream(device))
+                with torch.cuda.stream(warm), torch.inference_mode():
+                    model.step(self.input, self.cache)
+                torch.cuda.current_stream(device).wait_stream(warm)
+                self.graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.graph, stream=torch.cuda.Stream(device=device)), torch.inference_mode():
+                    self.output, updated = model.step(self.input, self.cache)
+                    for current, new in zip(self.cache, updated):
+                        for dst, src in zip(current, new):
+                            if dst.data_ptr() != src.data_ptr():
+                                dst.copy_(src)
+        finally:
+            for mixer in mixers:
+                mixer._state_in_place = False
+        self.reset()
+
+    def __call__(self, x: torch.Tensor, validate: bool = False) -> torch.Tensor:
+        if x.shape != self.input.shape:
+            raise ValueError(f"expected {tuple(self.input.shape)}, got {tuple(x.shape)}")
+        if x.device != self.input.device or x.dtype != self.input.dtype:
+            raise ValueError(f"expected {self.input.dtype} on {self.input.device}, got {x.dtype} on {x.device}")
+        if x.requires_grad:
+            raise ValueError("CUDA graph decoding does not support gradient inputs")
+        if validate:
+            self.validate()
+        with torch.inference_mode(), torch.cuda.device(self.input.device):
+            self.input.copy_(x)
+            self.graph.replay()
+        return self.output
+
+    def validate(self) -> None:
+        if self._parameter_signature() != self.parameter_signature:
+            raise RuntimeError("model state changed; recreate the CUDA graph decoder")
+
+    def reset(self) -> None:
+        for layer_cache in self.cache:
+            for tensor in layer_cache:
+                tensor.zero_()
+
+    def _parameter_signature(self):
+        return tuple((id(p), p._version, p.data_ptr(), p.device, p.dtype, tuple(p.shape))
+                     for p in self.model.parameters())

@@ -1,0 +1,69 @@
+"""The C-ABI library loads without a GPU, exports every entry point declared in include/*.h and
+rejects malformed arguments before touching the device."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from mamba3_b200 import _ext
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_functions() -> list[str]:
+    names = []
+    for header in sorted((ROOT / "include").glob("*.h")):
+        text = header.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"^\s*[A-Za-z_][\w \*]*?\b(m3_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _ext.load()
+    names = declared_functions()
+    assert {"m3_scan_fwd", "m3_step_fwd", "m3_last_error", "m3_abi_version"} <= set(names)
+    for name in names:
+        assert hasattr(lib, name), name
+    assert lib.m3_abi_version() == _ext.ABI_VERSION
+
+
+def test_struct_layout_matches_header():
+    # 12 ints + float + int, then 26 tensor descriptors of 64 bytes.
+    assert ctypes.sizeof(_ext.M3Tensor) == 64
+    assert ctypes.sizeof(_ext.ScanArgs) == 14 * 4 + 26 * 64
+    assert ctypes.sizeof(_ext.StepArgs) == 8 * 4 + 22 * 64
+
+
+def test_null_and_invalid_arguments_are_rejected_without_a_device():
+    lib = _ext.load()
+    assert lib.m3_scan_fwd(None, None) == 4
+    assert b"null" in lib.m3_last_error()
+    args = _ext.ScanArgs()
+    assert lib.m3_scan_fwd(ctypes.byref(args), None) == 1  # zero sizes
+    args.batch, args.length, args.groups, args.heads, args.rank, args.d_state, args.head_dim = 1, 4, 1, 2, 3, 8, 4
+    args.chunk_hint = 4
+    assert lib.m3_scan_fwd(ctypes.byref(args), None) == 1
+    assert b"rank" in lib.m3_last_error()
+    args.rank = 1
+    assert lib.m3_scan_fwd(ctypes.byref(args), None) == 4  # q missing
+    assert b"missing required tensor q" in lib.m3_last_error()
+    step = _ext.StepArgs()
+    step.batch, step.heads, step.rank, step.d_state, step.head_dim, step.num_angles = 1, 2, 4, 16, 8, 2
+    assert lib.m3_step_fwd(ctypes.byref(step), None) == 1
+    assert b"4 * num_angles" in lib.m3_last_error()
+
+
+def test_binding_refuses_host_tensors():
+    """The binding never runs anything on the CPU: host tensors are an error, not a fallback."""
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        _ext.scan_forward(sizes=dict(batch=1, length=2, groups=1, heads=1, rank=1, d_state=8, head_dim=4,
+                                     num_angles=0), tensors=dict(value=torch.empty(1)))
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        _ext.step_forward(sizes=dict(batch=1, heads=1, rank=1, d_state=8, head_dim=4, num_angles=2),
+                          tensors=dict(value=torch.empty(1)))

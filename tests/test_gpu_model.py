@@ -1,0 +1,178 @@
+"""GPU parity of the whole ``Mamba3`` drop-in (forward / prefill / step / cuda_graph) against the
+reference's golden outputs, and of the kernel path against the PyTorch formulation.
+
+Tolerances (normwise): float32 models <= 1e-4 against the reference outputs; bf16 autocast
+<= 2e-2 against the PyTorch formulation under the same autocast (the reference's portable path
+semantics) and <= 5e-2 against the float32 reference outputs.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import load_golden, rel_err
+from mamba3_b200 import Mamba3, _ext, ops
+from test_model_cpu import golden_model
+
+pytestmark = pytest.mark.gpu
+
+MODELS = ["model_r1", "model_r4", "model_n16_r1", "model_n16_r4", "model_bidir"]
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors():
+    yield
+    assert _ext.device_error(clear=True) == 0
+
+
+def run_continued(model, x, split):
+    prefix, cache = model.prefill(x[:, :split])
+    outs = [prefix]
+    for t in range(split, x.shape[1]):
+        o, cache = model.step(x[:, t:t + 1], cache)
+        outs.append(o)
+    return torch.cat(outs, dim=1), cache
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_fp32_model_matches_reference(name):
+    model, f = golden_model(name, device="cuda")
+    x = torch.from_numpy(f["x"]).cuda()
+    with torch.inference_mode():
+        y = model(x)
+        assert ops.LAST_SCAN_DISPATCH
+        assert rel_err(y, f["y"]) < 1e-4
+        if not model.causal:
+            return
+        cont, cache = run_continued(model, x, int(f["split"]))
+        assert ops.LAST_STEP_DISPATCH
+    assert rel_err(cont, f["continued"]) < 1e-4
+    for i, layer in enumerate(cache):
+        for j, tensor in enumerate(layer):
+            assert rel_err(tensor, f[f"cache{i}_{j}"]) < 2e-4, (i, j)
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_bf16_autocast_model(name):
+    model, f = golden_model(name, device="cuda")
+    x = torch.from_numpy(f["x"]).cuda()
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        y = model(x)
+    with torch.autocast("cuda", dtype=torch.bfloat16):  # grad mode on: the PyTorch formulation
+        for p in model.parameters():
+            p.requires_grad_(True)
+        y_torch = model(x).detach()
+    assert rel_err(y.float(), y_torch.float()) < 2e-2
+    assert rel_err(y.float(), f["y"]) < 5e-2
+    if model.causal:
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            cont, _ = run_continued(model, x, int(f["split"]))
+        assert rel_err(cont.float(), f["continued"]) < 5e-2
+
+
+@pytest.mark.parametrize("rank", [1, 4])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_low_precision_model_kernels_vs_pytorch(rank, dtype):
+    """Counterpart of the reference's fused-vs-portable test (tests/test_scan.py:385-435)."""
+    torch.manual_seed(11 + rank)
+    model = Mamba3(64, d_state=16, depth=1, mimo_rank=rank).cuda().to(dtype).eval()
+    x = torch.randn(2, 37, 64, device="cuda", dtype=dtype)
+    with torch.inference_mode():
+        actual = model(x)
+        cont, cache = run_continued(model, x, 9)
+    for p in model.parameters():
+        p.requires_grad_(True)
+    expected = model(x).detach()
+    torch.testing.assert_close(actual, expected, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(cont, expected, rtol=3e-2, atol=3e-2)
+
+
+def test_cuda_graph_decoder_matches_forward_and_resets():
+    torch.manual_seed(5)
+    model = Mamba3(64, d_state=128, depth=1).cuda().eval()
+    x = torch.randn(2, 5, 64, device="cuda")
+    ref_cache, ref_out = None, []
+    with torch.inference_mode():
+        for t in range(5):
+            o, ref_cache = model.step(x[:, t:t + 1], ref_cache)
+            ref_out.append(o)
+    decoder = model.cuda_graph(batch_size=2)
+    with torch.inference_mode():
+        expected = model(x)
+        actual = torch.cat([decoder(x[:, t:t + 1]).clone() for t in range(5)], dim=1)
+    torch.testing.assert_close(actual, expected, rtol=2e-4, atol=2e-5)
+    torch.testing.assert_close(actual, torch.cat(ref_out, 1), rtol=2e-4, atol=2e-5)
+    for graph_layer, ref_layer in zip(decoder.cache, ref_cache):
+        for a, b in zip(graph_layer, ref_layer):
+            torch.testing.assert_close(a, b, rtol=2e-4, atol=2e-5)
+    decoder.reset()
+    with torch.inference_mode():
+        again = decoder(x[:, :1]).clone()
+    torch.testing.assert_close(again, expected[:, :1], rtol=2e-4, atol=2e-5)
+    with torch.no_grad():
+        model.layers[0].mixer.D.add_(0.1)
+    with pytest.raises(RuntimeError, match="recreate"):
+        decoder.validate()
+    with pytest.raises(ValueError, match="gradient"):
+        decoder(x[:, :1].requires_grad_())
+
+
+@pytest.mark.parametrize("rank", [1, 4])
+def test_bf16_cuda_graph_decoder_matches_eager_steps(rank):
+    torch.manual_seed(21)
+    model = Mamba3(128, d_state=128, depth=2, mimo_rank=rank).cuda().to(torch.bfloat16).eval()
+    x = torch.randn(3, 6, 128, device="cuda", dtype=torch.bfloat16)
+    with torch.inference_mode():
+        _, cache = model.prefill(x[:, :2])
+        eager = []
+        for t in range(2, 6):
+            o, cache = model.step(x[:, t:t + 1], cache)
+            eager.append(o)
+    decoder = model.cuda_graph(batch_size=3)
+    with torch.inference_mode():
+        graph = [decoder(x[:, t:t + 1]).clone() for t in range(6)]
+        _, ref = model.prefill(x)
+    torch.testing.assert_close(torch.cat(graph, 1), model(x), rtol=3e-2, atol=3e-2)
+    for a, b in zip(decoder.cache, ref):
+        torch.testing.assert_close(a[1], b[1], rtol=3e-2, atol=3e-2)
+
+
+def test_autocast_dtypes_and_training_path_on_cuda():
+    torch.manual_seed(4)
+    model = Mamba3(64, d_state=16, depth=1).cuda()
+    x = torch.randn(2, 33, 64, device="cuda", requires_grad=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = model(x)
+    out.float().square().mean().backward()
+    assert out.dtype == torch.float32 and torch.isfinite(out).all()
+    assert all(p.grad is not None and torch.isfinite(p.grad).all() for p in model.parameters())
+    model.eval()
+    cache, steps = None, []
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        expected, prefill_cache = model.prefill(x.detach())
+        for t in range(x.shape[1]):
+            o, cache = model.step(x[:, t:t + 1].detach(), cache)
+            steps.append(o)
+    torch.testing.assert_close(torch.cat(steps, 1), expected, rtol=3e-2, atol=3e-2)
+    for a_layer, b_layer in zip(prefill_cache, cache):
+        for a, b in zip(a_layer, b_layer):
+            torch.testing.assert_close(a.float(), b.float(), rtol=3e-2, atol=3e-2)
+
+
+def test_negative_phase_increments_do_not_drift_at_long_context():
+    """The in-kernel blocked phase stays exact at L=131072 (tests/test_model.py:252-273)."""
+    import math
+    torch.manual_seed(0)
+    model = Mamba3(16, d_state=8, depth=1).cuda().eval()
+    mixer = model.layers[0].mixer
+    length = 131_072
+    raw = math.atanh(-1e-4 / math.pi)
+    angles = torch.full((1, length, mixer.num_angles), raw, device="cuda")
+    dt = torch.ones(1, length, mixer.nheads, device="cuda")
+    phase = mixer._phase(angles, dt, None)
+    inc = math.pi * math.tanh(raw)
+    pos = torch.arange(1, length + 1, device="cuda", dtype=torch.float64)
+    expected = torch.remainder(pos * inc, 2 * math.pi).float()[None, :, None, None].expand_as(phase)
+    circ = torch.remainder(phase - expected + math.pi, 2 * math.pi) - math.pi
+    assert circ.abs().max() < 2e-3
