@@ -2,8 +2,8 @@
 
 Tolerances (normwise: max|a-e| / max|e|):
   float32 activations: outputs and states <= 1e-4 (north-star fp32 bound)
-  bf16 / fp16 activations: outputs <= 2e-2, FP32 states <= 5e-3, against the float64 oracle run
-  on the same low-precision-rounded inputs.
+  bf16 / fp16 activations: outputs <= 2e-2, FP32 states <= 1e-2 (bf16) / 5e-3 (fp16), against
+  the float64 oracle run on the same low-precision-rounded inputs.
 """
 
 from __future__ import annotations
@@ -21,6 +21,7 @@ from test_oracle_golden import oracle_scan_inputs
 pytestmark = pytest.mark.gpu
 
 LOW = [torch.bfloat16, torch.float16]
+STATE_TOL = {torch.bfloat16: 1e-2, torch.float16: 5e-3, torch.float32: 1e-4}
 
 
 @pytest.fixture(autouse=True)
@@ -60,7 +61,7 @@ def test_scan_low_precision_matches_oracle(name, dtype):
     q, k, okw = oracle_scan_inputs(f)
     ye, se = O.scan_recurrent(q, k, f["value"], f["gate"], f["adt"], f["dt"], f["trap"], f["D"], **okw)
     assert rel_err(y.float(), ye) < 2e-2
-    assert rel_err(s, se) < 5e-3
+    assert rel_err(s, se) < STATE_TOL[dtype]
 
 
 def _random_scan(batch, length, heads, rank, n, p, s_angles, seed, device="cuda", cache=True, groups=1):
@@ -99,7 +100,7 @@ def test_scan_ragged_lengths_against_oracle(rank, length, dtype):
     f.update({key: to_np(val) for key, val in kwl.items() if isinstance(val, torch.Tensor)})
     q, k, okw = oracle_scan_inputs(f)
     ye, se = O.scan_chunked(q, k, f["value"], f["gate"], f["adt"], f["dt"], f["trap"], f["D"], chunk_size=64, **okw)
-    tol_y, tol_s = (1e-4, 1e-4) if dtype == torch.float32 else (2e-2, 5e-3)
+    tol_y, tol_s = (1e-4 if dtype == torch.float32 else 2e-2), STATE_TOL[dtype]
     assert rel_err(y.float(), ye) < tol_y
     assert rel_err(s, se) < tol_s
 
@@ -125,7 +126,7 @@ def test_scan_continuation_at_length_4096(rank):
         k2 = dict(kw, phase=kw["phase"][:, m:], initial_state=s1, initial_k=kx[:, 0], initial_value=args[2][:, m - 1])
         y2, s2 = ops.mamba3_scan(*second, **k2)
     assert rel_err(torch.cat((y1, y2), 1).float(), full.float()) < 2e-2
-    assert rel_err(s2, full_s) < 5e-3
+    assert rel_err(s2, full_s) < STATE_TOL[torch.bfloat16]
 
 
 @pytest.mark.parametrize("rank", [1, 4])
@@ -155,7 +156,7 @@ def test_step_matches_reference_fixture(rank, dtype):
                                         g["angle_rate"], g["D"], (g["phase0"], g["state0"], g["k0"], g["v0"]),
                                         mimo_x=g.get("mimo_x"), mimo_z=g.get("mimo_z"), mimo_out=g.get("mimo_out"))
     assert rel_err(y.float(), ye) < 2e-2
-    assert rel_err(s, se) < 5e-3
+    assert rel_err(s, se) < STATE_TOL[dtype]
     assert rel_err(k1.float(), ke) < 2e-2
     assert rel_err(ph, phe) < 1e-5
 
