@@ -72,6 +72,9 @@ typedef struct m3_tensor {
  *   initial_state   [B,H,P,N]    float32, optional
  *   initial_k       [B,H,R,N]    optional endpoint cache (rotated previous k)
  *   initial_value   [B,H,P]      optional endpoint cache (previous value)
+ *   workspace       float32 scratch of m3_scan_workspace_bytes(args) bytes (contiguous), required
+ *                   when that size is non-zero: per-token values shared by all heads (RMS factors
+ *                   of q/k rows, pi*tanh(angle)) computed once by a pre-pass instead of per head
  * Outputs:
  *   y               [B,L,H,P]    activation dtype
  *   final_state     [B,H,P,N]    float32
@@ -93,6 +96,7 @@ typedef struct m3_scan_args {
   m3_tensor D, mimo_x, mimo_z, mimo_out;
   m3_tensor initial_state, initial_k, initial_value;
   m3_tensor y, final_state, final_phase, final_k;
+  m3_tensor workspace;
 } m3_scan_args;
 
 /*
@@ -122,6 +126,9 @@ typedef struct m3_step_args {
 
 /* Chunked SSD forward. Returns M3_OK or an M3_ERR_* code. */
 int m3_scan_fwd(const m3_scan_args* args, void* stream);
+
+/* Bytes of float32 workspace m3_scan_fwd needs for these arguments (0 = none). */
+int64_t m3_scan_workspace_bytes(const m3_scan_args* args);
 
 /* Decode step. Returns M3_OK or an M3_ERR_* code. */
 int m3_step_fwd(const m3_step_args* args, void* stream);

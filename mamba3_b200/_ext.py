@@ -37,6 +37,7 @@ _SCAN_TENSORS = (
     "D", "mimo_x", "mimo_z", "mimo_out",
     "initial_state", "initial_k", "initial_value",
     "y", "final_state", "final_phase", "final_k",
+    "workspace",
 )
 
 _STEP_TENSORS = (
@@ -91,6 +92,8 @@ def load() -> ctypes.CDLL:
         lib.m3_abi_version.restype = ctypes.c_int
         lib.m3_device_error.argtypes = [ctypes.c_int]
         lib.m3_device_error.restype = ctypes.c_int
+        lib.m3_scan_workspace_bytes.argtypes = [ctypes.POINTER(ScanArgs)]
+        lib.m3_scan_workspace_bytes.restype = ctypes.c_int64
         lib.m3_last_scan_kernel.argtypes = []
         lib.m3_last_scan_kernel.restype = ctypes.c_char_p
         if lib.m3_abi_version() != ABI_VERSION:
@@ -147,6 +150,13 @@ def scan_forward(*, sizes: dict, tensors: dict, reverse: bool = False, mimo_rota
     args.device = device.index if device.index is not None else torch.cuda.current_device()
     for name in _SCAN_TENSORS:
         setattr(args, name, _desc(tensors.get(name)))
+    need = lib.m3_scan_workspace_bytes(ctypes.byref(args))
+    if need < 0:
+        _check(int(-need), lib)
+    workspace = None
+    if need > 0:
+        workspace = torch.empty((need + 3) // 4, device=device, dtype=torch.float32)
+        args.workspace = _desc(workspace)
     stream = torch.cuda.current_stream(device).cuda_stream
     _check(lib.m3_scan_fwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
 

@@ -12,6 +12,7 @@ cudaError_t launch_step(const m3_step_args& a, cudaStream_t stream);
 cudaError_t launch_scan_simt(const m3_scan_args& a, cudaStream_t stream);
 size_t scan_simt_smem_bytes(int rank, int N, int P, int S);
 bool scan_umma_supported(const m3_scan_args& a);
+int64_t scan_umma_workspace_bytes(const m3_scan_args& a);
 cudaError_t launch_scan_umma(const m3_scan_args& a, cudaStream_t stream);
 }  // namespace m3
 
@@ -110,6 +111,11 @@ int m3_step_fwd(const m3_step_args* args, void* stream) {
   return M3_OK;
 }
 
+int64_t m3_scan_workspace_bytes(const m3_scan_args* args) {
+  if (args == nullptr) return -fail(M3_ERR_ARGUMENT, "null argument struct");
+  return m3::scan_umma_supported(*args) ? m3::scan_umma_workspace_bytes(*args) : 0;
+}
+
 int m3_scan_fwd(const m3_scan_args* args, void* stream) {
   M3_REQUIRE(args != nullptr, M3_ERR_ARGUMENT, "null argument struct");
   const m3_scan_args& a = *args;
@@ -136,6 +142,7 @@ int m3_scan_fwd(const m3_scan_args* args, void* stream) {
       {&a.initial_k, "initial_k", 4, false}, {&a.initial_value, "initial_value", 3, false},
       {&a.y, "output", 4, true}, {&a.final_state, "final_state", 4, true},
       {&a.final_phase, "final_phase", 3, false}, {&a.final_k, "final_k", 4, false},
+      {&a.workspace, "workspace", 1, false},
   };
   for (const Item& it : items) {
     const int rc = check_tensor(*it.t, it.name, it.nd, it.req);
@@ -161,6 +168,9 @@ int m3_scan_fwd(const m3_scan_args* args, void* stream) {
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (m3::scan_umma_supported(a)) {
+    const int64_t need = m3::scan_umma_workspace_bytes(a);
+    M3_REQUIRE(need == 0 || (present(a.workspace) && a.workspace.dtype == M3_F32), M3_ERR_ARGUMENT,
+               "a float32 workspace of m3_scan_workspace_bytes() bytes is required");
     g_last_scan_kernel = "umma";
     e = m3::launch_scan_umma(a, s);
   } else {

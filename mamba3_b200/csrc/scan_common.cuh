@@ -46,43 +46,53 @@ struct TileScalars {
   float* scale;
   float* diag;
   float* dt;     // dt of each tile token (phase increments)
-  float* wsum;   // >= 4 floats scratch (warp totals of the scan)
+  float* wsum;   // >= 8 floats scratch (warp totals of the scan, look-ahead token)
 };
 
-// Fill the per-token scalars of tile [t0, t0 + nt) (scan order). Threads >= 128 idle.
-// Requires TOK <= 128 and blockDim.x >= 128. Ends with __syncthreads().
+// Fill the per-token scalars of tile [t0, t0 + nt) (scan order). All loads are issued in one
+// parallel round (thread j loads token j; one extra thread loads the first token after the tile).
+// Requires TOK <= 128 and blockDim.x >= 160. Ends with __syncthreads().
 __device__ inline void tile_scalars(const m3_scan_args& a, int b, int h, int t0, int nt, int TOK,
                                     const TileScalars& s, float& last_decay) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
-  float adtv = 0.0f;
-  if (tid < TOK) {
-    float dtv = 0.0f, scale = 0.0f, diag = 0.0f;
-    if (tid < nt) {
-      const int ts = t0 + tid;
-      const int t = scan_token(a, ts);
+  // Round 1: raw per-token values. adt is parked in `cum`, sigma in `edec`.
+  if (tid <= TOK) {
+    float dtv = 0.0f, adtv = 0.0f, sg = 0.0f;
+    if (t0 + tid < a.length && (tid < nt || tid == TOK)) {
+      const int t = scan_token(a, t0 + tid);
       load_dt_adt(a, b, t, h, dtv, adtv);
-      const float sg = sigmoidf_(load_trap(a, b, t, h));
-      const float gamma = dtv * sg;
-      float nxt = 0.0f;
-      if (ts + 1 < a.length) {
-        const int tn = scan_token(a, ts + 1);
-        float dtn, adtn;
-        load_dt_adt(a, b, tn, h, dtn, adtn);
-        nxt = dtn * (1.0f - sigmoidf_(load_trap(a, b, tn, h)));
-      }
-      scale = gamma + nxt;
-      diag = gamma / scale;
+      sg = sigmoidf_(load_trap(a, b, t, h));
     }
-    s.dt[tid] = dtv;
-    s.scale[tid] = scale;
-    s.diag[tid] = diag;
+    if (tid < TOK) {
+      s.dt[tid] = tid < nt ? dtv : 0.0f;
+      s.cum[tid] = tid < nt ? adtv : 0.0f;
+      s.edec[tid] = sg;
+    } else {
+      s.wsum[4] = dtv;
+      s.wsum[5] = sg;
+    }
   }
-  // Inclusive scan of adt over the tile (4 warps x 32).
+  __syncthreads();
+  // Round 2: trapezoid scalars and the inclusive scan of adt (4 warps x 32).
   float v = 0.0f;
   if (tid < 128) {
+    const float adtv = tid < TOK ? s.cum[tid] : 0.0f;
     v = warp_incl_scan(adtv, lane);
     if (lane == 31) s.wsum[tid >> 5] = v;
+    if (tid < TOK) {
+      float scale = 0.0f, diag = 0.0f;
+      if (tid < nt) {
+        const float gamma = s.dt[tid] * s.edec[tid];
+        float nxt = 0.0f;
+        if (tid + 1 < nt) nxt = s.dt[tid + 1] * (1.0f - s.edec[tid + 1]);
+        else if (t0 + tid + 1 < a.length) nxt = s.wsum[4] * (1.0f - s.wsum[5]);
+        scale = gamma + nxt;
+        diag = gamma / scale;
+      }
+      s.scale[tid] = scale;
+      s.diag[tid] = diag;
+    }
   }
   __syncthreads();
   if (tid < TOK) {
@@ -107,9 +117,9 @@ __device__ inline void tile_scalars(const m3_scan_args& a, int b, int h, int t0,
 //    fmod(pi tanh(angle) dt, 2pi) summed from the start of each 64-token block, the block offset
 //    carried in `carry_off` and reduced mod 2pi at every block end; the running within-block sum
 //    is carried across tiles in `carry_loc` (tiles may be shorter than a block).
-// `seg_buf` needs 3 * 256 floats; TOK is a power of two <= 128 and blockDim.x == 256, so each
-// segment of SL tokens lies inside one 64-token block.
-// Ends with __syncthreads().
+// `seg_buf` needs 3 * 256 floats; TOK is a power of two <= 128 and blockDim.x >= 256 (only the
+// first 256 threads take part in the segment sums), so each segment of SL tokens lies inside one
+// 64-token block. Ends with __syncthreads().
 __device__ inline void tile_phase(const m3_scan_args& a, int b, int h, int t0, int nt, int TOK, const float* s_dt,
                                   float* s_ph, int ph_stride, float* carry_off, float* carry_loc, float* seg_buf) {
   const int S = a.num_angles;
@@ -128,28 +138,34 @@ __device__ inline void tile_phase(const m3_scan_args& a, int b, int h, int t0, i
     __syncthreads();
     return;
   }
-  // S_pad threads per segment row; nseg segments of SL tokens each.
+  // Round 1: every increment, loads issued in parallel (consecutive threads -> consecutive angles).
+  for (int i = tid; i < TOK * S; i += blockDim.x) {
+    const int j = i / S, sidx = i % S;
+    float inc = 0.0f;
+    if (j < nt) {
+      const int t = scan_token(a, t0 + j);
+      const float th = ld_t(a.angles, b * a.angles.stride[0] + (int64_t)t * a.angles.stride[1] +
+                                          sidx * a.angles.stride[2]);
+      inc = fmodf((kPi * tanhf(th)) * s_dt[j], kTwoPi);
+    }
+    s_ph[j * ph_stride + sidx] = inc;
+  }
+  __syncthreads();
+  // Round 2: segment-local inclusive sums (S_pad threads per segment row, nseg segments).
   int S_pad = 1;
   while (S_pad < S) S_pad <<= 1;
-  const int nseg_max = (int)blockDim.x / S_pad;
+  const int nseg_max = 256 / S_pad;
   int nseg = 1;
-  while (nseg * 2 <= nseg_max && TOK % (nseg * 2) == 0 && TOK / (nseg * 2) >= 1) nseg <<= 1;
-  const int SL = TOK / nseg;  // divides 64 because TOK and nseg are powers of two and SL <= 64 is ensured
+  while (nseg * 2 <= nseg_max && TOK % (nseg * 2) == 0) nseg <<= 1;
+  const int SL = TOK / nseg;
   const int sidx = tid % S_pad;
   const int seg = tid / S_pad;
-  float local = 0.0f;
-  const bool active = sidx < S && seg < nseg;
+  const bool active = tid < 256 && sidx < S && seg < nseg;
   if (active) {
+    float local = 0.0f;
     for (int j = seg * SL; j < (seg + 1) * SL; ++j) {
-      float inc = 0.0f;
-      if (j < nt) {
-        const int t = scan_token(a, t0 + j);
-        const float th = ld_t(a.angles, b * a.angles.stride[0] + (int64_t)t * a.angles.stride[1] +
-                                            sidx * a.angles.stride[2]);
-        inc = fmodf((kPi * tanhf(th)) * s_dt[j], kTwoPi);
-      }
-      local += inc;
-      s_ph[j * ph_stride + sidx] = local;  // segment-local inclusive prefix
+      local += s_ph[j * ph_stride + sidx];
+      s_ph[j * ph_stride + sidx] = local;
     }
     seg_buf[seg * S_pad + sidx] = local;
   }
@@ -157,8 +173,8 @@ __device__ inline void tile_phase(const m3_scan_args& a, int b, int h, int t0, i
   if (tid < S) {
     float off = carry_off[tid], loc = carry_loc[tid];
     for (int sg = 0; sg < nseg; ++sg) {
-      const int g = t0 + sg * SL;
-      if (g > 0 && (g % kPhaseBlock) == 0) {  // a new 64-token block starts here
+      const int gi = t0 + sg * SL;
+      if (gi > 0 && (gi % kPhaseBlock) == 0) {  // a new 64-token block starts here
         off = fmodf(off + loc, kTwoPi);
         loc = 0.0f;
       }
