@@ -130,6 +130,22 @@ int m3_scan_fwd(const m3_scan_args* args, void* stream);
 /* Bytes of float32 workspace m3_scan_fwd needs for these arguments (0 = none). */
 int64_t m3_scan_workspace_bytes(const m3_scan_args* args);
 
+/* Fixed scratch size of m3_scan_fwd_noalloc, per GPU that loads the library: 8 MiB. */
+#define M3_NOALLOC_WORKSPACE_BYTES (8 * 1024 * 1024)
+
+/*
+ * Chunked SSD forward that allocates nothing, for callers that cannot call cudaMalloc where they
+ * run the scan (a host runtime that owns all device memory through its own pool, a plugin that
+ * must not touch its host process's allocator). Same arguments and results as m3_scan_fwd, but
+ * args->workspace is ignored: the scratch is a fixed array inside the library's device image,
+ * M3_NOALLOC_WORKSPACE_BYTES per GPU, held until process exit. Sizes whose scratch
+ * (m3_scan_workspace_bytes) exceeds that limit are rejected with M3_ERR_SHAPE. The first call on
+ * a device looks up the array's device address once; make that first call before any stream
+ * capture. All calls share the one array, so calls on one device that overlap on the GPU race on
+ * it; calls ordered on one stream are safe. Has no counterpart in the reference.
+ */
+int m3_scan_fwd_noalloc(const m3_scan_args* args, void* stream);
+
 /* Decode step. Returns M3_OK or an M3_ERR_* code. */
 int m3_step_fwd(const m3_step_args* args, void* stream);
 

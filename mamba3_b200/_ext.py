@@ -182,3 +182,27 @@ def last_scan_kernel() -> str:
 
 def device_error(clear: bool = True) -> int:
     return load().m3_device_error(int(clear))
+
+
+@torch.compiler.disable
+def scan_forward_noalloc(*, sizes: dict, tensors: dict, reverse: bool = False, mimo_rotation: bool = False,
+                         chunk_hint: int = 64, norm_eps: float = 1e-5) -> None:
+    """Enqueue ``m3_scan_fwd_noalloc``: the scan with the library's fixed scratch array instead of a
+    caller workspace, for hosts that cannot allocate device memory at the call site (see the
+    header). Nothing is allocated here either."""
+    lib = load()
+    lib.m3_scan_fwd_noalloc.argtypes = [ctypes.POINTER(ScanArgs), ctypes.c_void_p]
+    lib.m3_scan_fwd_noalloc.restype = ctypes.c_int
+    args = ScanArgs()
+    for key, val in sizes.items():
+        setattr(args, key, int(val))
+    args.reverse = int(reverse)
+    args.mimo_rotation = int(mimo_rotation)
+    args.chunk_hint = int(chunk_hint)
+    args.norm_eps = float(norm_eps)
+    device = _cuda_device(tensors)
+    args.device = device.index if device.index is not None else torch.cuda.current_device()
+    for name in _SCAN_TENSORS:
+        setattr(args, name, _desc(tensors.get(name)))
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _check(lib.m3_scan_fwd_noalloc(ctypes.byref(args), ctypes.c_void_p(stream)), lib)

@@ -57,6 +57,11 @@ int select_device(int device) {
 
 }  // namespace
 
+namespace m3 {
+// Record `msg` as this thread's m3_last_error() and return `code` (for other translation units).
+int report_error(int code, const char* msg) { return fail(code, msg); }
+}  // namespace m3
+
 extern "C" {
 
 const char* m3_last_error(void) { return g_last_error.c_str(); }
