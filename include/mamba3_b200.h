@@ -113,6 +113,9 @@ typedef struct m3_scan_args {
  * Outputs: y [B,H,P]; out_phase [B,H,S] f32; out_state [B,H,P,N] f32 (may alias `state`
  * exactly, for in-place decoding); out_k [B,H,R,N] (rotated k). out_phase/out_k must not
  * alias phase/prev_k.
+ *   workspace   float32 scratch of m3_step_workspace_bytes(args) bytes (contiguous), required
+ *               when that size is non-zero: the per-(batch, head) rotated q/k and decay scalars
+ *               a pre-pass computes so that the state pass is a pure stream over HBM
  */
 typedef struct m3_step_args {
   int32_t batch, heads, rank, d_state, head_dim, num_angles;
@@ -122,6 +125,7 @@ typedef struct m3_step_args {
   m3_tensor adt, dt, trap, angle_rate, D, mimo_x, mimo_z, mimo_out;
   m3_tensor phase, state, prev_k, prev_value;
   m3_tensor y, out_phase, out_state, out_k;
+  m3_tensor workspace;
 } m3_step_args;
 
 /* Chunked SSD forward. Returns M3_OK or an M3_ERR_* code. */
@@ -148,6 +152,9 @@ int m3_scan_fwd_noalloc(const m3_scan_args* args, void* stream);
 
 /* Decode step. Returns M3_OK or an M3_ERR_* code. */
 int m3_step_fwd(const m3_step_args* args, void* stream);
+
+/* Bytes of float32 workspace m3_step_fwd needs for these arguments (0 = none). */
+int64_t m3_step_workspace_bytes(const m3_step_args* args);
 
 /* Message for the last non-zero status returned on this host thread. */
 const char* m3_last_error(void);

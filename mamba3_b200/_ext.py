@@ -45,6 +45,7 @@ _STEP_TENSORS = (
     "adt", "dt", "trap", "angle_rate", "D", "mimo_x", "mimo_z", "mimo_out",
     "phase", "state", "prev_k", "prev_value",
     "y", "out_phase", "out_state", "out_k",
+    "workspace",
 )
 
 
@@ -94,6 +95,8 @@ def load() -> ctypes.CDLL:
         lib.m3_device_error.restype = ctypes.c_int
         lib.m3_scan_workspace_bytes.argtypes = [ctypes.POINTER(ScanArgs)]
         lib.m3_scan_workspace_bytes.restype = ctypes.c_int64
+        lib.m3_step_workspace_bytes.argtypes = [ctypes.POINTER(StepArgs)]
+        lib.m3_step_workspace_bytes.restype = ctypes.c_int64
         lib.m3_last_scan_kernel.argtypes = []
         lib.m3_last_scan_kernel.restype = ctypes.c_char_p
         if lib.m3_abi_version() != ABI_VERSION:
@@ -172,6 +175,13 @@ def step_forward(*, sizes: dict, tensors: dict) -> None:
     args.device = device.index if device.index is not None else torch.cuda.current_device()
     for name in _STEP_TENSORS:
         setattr(args, name, _desc(tensors.get(name)))
+    need = lib.m3_step_workspace_bytes(ctypes.byref(args))
+    if need < 0:
+        _check(int(-need), lib)
+    workspace = None
+    if need > 0:
+        workspace = torch.empty((need + 3) // 4, device=device, dtype=torch.float32)
+        args.workspace = _desc(workspace)
     stream = torch.cuda.current_stream(device).cuda_stream
     _check(lib.m3_step_fwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
 

@@ -9,6 +9,7 @@ namespace m3 {
 int read_device_error(int clear);
 
 cudaError_t launch_step(const m3_step_args& a, cudaStream_t stream);
+int64_t step_workspace_bytes(const m3_step_args& a);
 cudaError_t launch_scan_simt(const m3_scan_args& a, cudaStream_t stream);
 size_t scan_simt_smem_bytes(int rank, int N, int P, int S);
 bool scan_umma_supported(const m3_scan_args& a);
@@ -72,6 +73,11 @@ const char* m3_last_scan_kernel(void) { return g_last_scan_kernel; }
 
 int m3_device_error(int clear) { return m3::read_device_error(clear); }
 
+int64_t m3_step_workspace_bytes(const m3_step_args* args) {
+  if (args == nullptr) return -fail(M3_ERR_ARGUMENT, "null argument struct");
+  return m3::step_workspace_bytes(*args);
+}
+
 int m3_step_fwd(const m3_step_args* args, void* stream) {
   M3_REQUIRE(args != nullptr, M3_ERR_ARGUMENT, "null argument struct");
   const m3_step_args& a = *args;
@@ -92,7 +98,7 @@ int m3_step_fwd(const m3_step_args* args, void* stream) {
       {&a.mimo_out, "mimo_out", 3, a.rank > 1}, {&a.phase, "phase", 3, true}, {&a.state, "state", 4, true},
       {&a.prev_k, "previous_k", 4, true}, {&a.prev_value, "previous_value", 3, true}, {&a.y, "output", 3, true},
       {&a.out_phase, "output_phase", 3, true}, {&a.out_state, "output_state", 4, true},
-      {&a.out_k, "output_k", 4, true},
+      {&a.out_k, "output_k", 4, true}, {&a.workspace, "workspace", 1, false},
   };
   for (const Item& it : items) {
     const int rc = check_tensor(*it.t, it.name, it.nd, it.req);
@@ -109,9 +115,14 @@ int m3_step_fwd(const m3_step_args* args, void* stream) {
   M3_REQUIRE(a.rank > 1 || !present(a.mimo_x), M3_ERR_ARGUMENT, "MIMO projections require rank > 1");
   M3_REQUIRE(a.out_phase.data != a.phase.data && a.out_k.data != a.prev_k.data, M3_ERR_LAYOUT,
              "output phase / k must not alias the input cache");
+  const int64_t need = m3::step_workspace_bytes(a);
+  M3_REQUIRE(need == 0 || (present(a.workspace) && a.workspace.dtype == M3_F32), M3_ERR_ARGUMENT,
+             "a float32 workspace of m3_step_workspace_bytes() bytes is required");
+  m3_step_args run = a;
+  if (need == 0) run.workspace = m3_tensor{};
   const int dev_rc = select_device(a.device);
   if (dev_rc != M3_OK) return dev_rc;
-  const cudaError_t e = m3::launch_step(a, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = m3::launch_step(run, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("step launch failed: ") + cudaGetErrorString(e));
   return M3_OK;
 }

@@ -17,92 +17,152 @@
 namespace m3 {
 
 constexpr int kStepThreads = 128;
+#ifndef M3_STEP_BIG_ROWS
+#define M3_STEP_BIG_ROWS 8
+#endif
+constexpr int kStepBigRows = M3_STEP_BIG_ROWS;  // state rows per warp in the stream pass at large batch
 
-template <typename T, int R, int NPL>
-__global__ void __launch_bounds__(kStepThreads) step_kernel(const m3_step_args a, int rows_per_cta) {
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int p0 = blockIdx.x * rows_per_cta;
-  const int N = a.d_state, P = a.head_dim, S = a.num_angles;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  extern __shared__ float sm[];
+// Per-(batch, head) prologue shared by both step kernels: new phase (written by the CTA with
+// write_small), rotated q/k into s_q/s_k (activation-rounded), previous k into s_kp, and the
+// scalars alpha, beta, gamma, D. Ends with __syncthreads().
+struct StepScalars {
+  float alpha, beta, gamma, Dh;
+};
+
+template <typename T, int R>
+__device__ __forceinline__ StepScalars step_prologue(const m3_step_args& a, int b, int h, bool write_small, float* sm) {
+  // Every global load of the prologue is issued first (one memory round trip), then the math.
+  constexpr int kPairIters = R;      // R * (N / 2) <= 128 R pairs for N <= 256, 128 threads
+  constexpr int kPrevIters = 2 * R;  // R * N <= 256 R elements
+  const int N = a.d_state, S = a.num_angles;
+  const int tid = threadIdx.x;
+  const int half = N / 2;
   float* s_cos = sm;            // S
   float* s_sin = sm + 64;       // S
   float* s_q = sm + 128;        // R * N   rotated q (activation-rounded)
   float* s_k = s_q + R * N;     // R * N   rotated k
   float* s_kp = s_k + R * N;    // R * N   previous rotated k (cache)
-  const bool write_small = blockIdx.x == 0;
+  const T* qp = static_cast<const T*>(a.q.data);
+  const T* kp = static_cast<const T*>(a.k.data);
 
   const float dtv = ld_t(a.dt, b * a.dt.stride[0] + h * a.dt.stride[1]);
-  for (int s = tid; s < S; s += blockDim.x) {
-    const float th = ld_t(a.angle_rate, b * a.angle_rate.stride[0] + s * a.angle_rate.stride[1]);
+  const float adtv = ld_t(a.adt, b * a.adt.stride[0] + h * a.adt.stride[1]);
+  const float trapv = ld_t(a.trap, b * a.trap.stride[0] + h * a.trap.stride[1]);
+  const float Dh = ld_t(a.D, h * a.D.stride[0]);
+  float th = 0.0f, old = 0.0f;
+  if (tid < S) {
+    th = ld_t(a.angle_rate, b * a.angle_rate.stride[0] + tid * a.angle_rate.stride[1]);
+    old = ld_t(a.phase, b * a.phase.stride[0] + h * a.phase.stride[1] + tid * a.phase.stride[2]);
+  }
+  // Rotation pairs (e0, e1) — SISO (2m, 2m+1), MIMO (m, m + N/2) — so both elements of a pair
+  // are in the same thread.
+  float q0[kPairIters], q1[kPairIters], k0[kPairIters], k1[kPairIters];
+#pragma unroll
+  for (int j = 0; j < kPairIters; ++j) {
+    const int i = tid + j * kStepThreads;
+    q0[j] = q1[j] = k0[j] = k1[j] = 0.0f;
+    if (i < R * half) {
+      const int r = i / half, m = i % half;
+      const int e0 = R > 1 ? m : 2 * m;
+      const int e1 = R > 1 ? m + half : 2 * m + 1;
+      const int64_t qb = b * a.q.stride[0] + h * a.q.stride[1] + r * a.q.stride[2];
+      const int64_t kb = b * a.k.stride[0] + h * a.k.stride[1] + r * a.k.stride[2];
+      q0[j] = to_f(qp[qb + e0 * a.q.stride[3]]);
+      q1[j] = to_f(qp[qb + e1 * a.q.stride[3]]);
+      k0[j] = to_f(kp[kb + e0 * a.k.stride[3]]);
+      k1[j] = to_f(kp[kb + e1 * a.k.stride[3]]);
+      if (a.q_bias.data) {
+        const m3_tensor& qb_ = a.q_bias;
+        const m3_tensor& kb_ = a.k_bias;
+        const int64_t qo = h * qb_.stride[0] + r * qb_.stride[1];
+        const int64_t ko = h * kb_.stride[0] + r * kb_.stride[1];
+        q0[j] = rnd<T>(q0[j] + rnd<T>(ld_t(qb_, qo + e0 * qb_.stride[2])));
+        q1[j] = rnd<T>(q1[j] + rnd<T>(ld_t(qb_, qo + e1 * qb_.stride[2])));
+        k0[j] = rnd<T>(k0[j] + rnd<T>(ld_t(kb_, ko + e0 * kb_.stride[2])));
+        k1[j] = rnd<T>(k1[j] + rnd<T>(ld_t(kb_, ko + e1 * kb_.stride[2])));
+      }
+    }
+  }
+  float kprev[kPrevIters];
+#pragma unroll
+  for (int j = 0; j < kPrevIters; ++j) {
+    const int i = tid + j * kStepThreads;
+    kprev[j] = 0.0f;
+    if (i < R * N) {
+      const int r = i / N, n = i % N;
+      const m3_tensor& t = a.prev_k;
+      kprev[j] = ld_t(t, b * t.stride[0] + h * t.stride[1] + r * t.stride[2] + n * t.stride[3]);
+    }
+  }
+
+  if (tid < S) {
     const float inc = fmodf((kPi * tanhf(th)) * dtv, kTwoPi);
-    const float old = ld_t(a.phase, b * a.phase.stride[0] + h * a.phase.stride[1] + s * a.phase.stride[2]);
     const float ph = fmodf(old + inc, kTwoPi);
     if (write_small) {
       const m3_tensor& o = a.out_phase;
-      static_cast<float*>(o.data)[b * o.stride[0] + h * o.stride[1] + s * o.stride[2]] = ph;
+      static_cast<float*>(o.data)[b * o.stride[0] + h * o.stride[1] + tid * o.stride[2]] = ph;
     }
     float sn, cs;
     sincosf(ph, &sn, &cs);
-    s_cos[s] = rnd<T>(cs);
-    s_sin[s] = rnd<T>(sn);
+    s_cos[tid] = rnd<T>(cs);
+    s_sin[tid] = rnd<T>(sn);
+  }
+#pragma unroll
+  for (int j = 0; j < kPrevIters; ++j) {
+    const int i = tid + j * kStepThreads;
+    if (i < R * N) s_kp[i] = kprev[j];
   }
   __syncthreads();
-  // Rotated q/k: each thread owns rotation pairs (e0, e1) — SISO (2m, 2m+1), MIMO (m, m + N/2)
-  // — so the partner element is always in the same thread.
-  const T* qp = static_cast<const T*>(a.q.data);
-  const T* kp = static_cast<const T*>(a.k.data);
-  const int half = N / 2;
-  for (int i = tid; i < R * half; i += blockDim.x) {
-    const int r = i / half, m = i % half;
-    const int e0 = R > 1 ? m : 2 * m;
-    const int e1 = R > 1 ? m + half : 2 * m + 1;
-    const int64_t qb = b * a.q.stride[0] + h * a.q.stride[1] + r * a.q.stride[2];
-    const int64_t kb = b * a.k.stride[0] + h * a.k.stride[1] + r * a.k.stride[2];
-    float q0 = to_f(qp[qb + e0 * a.q.stride[3]]), q1 = to_f(qp[qb + e1 * a.q.stride[3]]);
-    float k0 = to_f(kp[kb + e0 * a.k.stride[3]]), k1 = to_f(kp[kb + e1 * a.k.stride[3]]);
-    if (a.q_bias.data) {
-      const m3_tensor& qb_ = a.q_bias;
-      const m3_tensor& kb_ = a.k_bias;
-      const int64_t qo = h * qb_.stride[0] + r * qb_.stride[1];
-      const int64_t ko = h * kb_.stride[0] + r * kb_.stride[1];
-      q0 = rnd<T>(q0 + rnd<T>(ld_t(qb_, qo + e0 * qb_.stride[2])));
-      q1 = rnd<T>(q1 + rnd<T>(ld_t(qb_, qo + e1 * qb_.stride[2])));
-      k0 = rnd<T>(k0 + rnd<T>(ld_t(kb_, ko + e0 * kb_.stride[2])));
-      k1 = rnd<T>(k1 + rnd<T>(ld_t(kb_, ko + e1 * kb_.stride[2])));
-    }
-    // SISO rotates pairs m < S; MIMO rotates (m, m + 2S) for m < S, and 2S == N/2 there.
-    if (m < S) {
-      const float cs = s_cos[m], sn = s_sin[m];
-      const float nq0 = rnd<T>(rnd<T>(q0 * cs) - rnd<T>(q1 * sn));
-      const float nq1 = rnd<T>(rnd<T>(q0 * sn) + rnd<T>(q1 * cs));
-      const float nk0 = rnd<T>(rnd<T>(k0 * cs) - rnd<T>(k1 * sn));
-      const float nk1 = rnd<T>(rnd<T>(k0 * sn) + rnd<T>(k1 * cs));
-      q0 = nq0; q1 = nq1; k0 = nk0; k1 = nk1;
-    }
-    s_q[r * N + e0] = q0;
-    s_q[r * N + e1] = q1;
-    s_k[r * N + e0] = k0;
-    s_k[r * N + e1] = k1;
-    if (write_small) {
-      const m3_tensor& o = a.out_k;
-      T* op = static_cast<T*>(o.data);
-      const int64_t ob = b * o.stride[0] + h * o.stride[1] + r * o.stride[2];
-      op[ob + e0 * o.stride[3]] = from_f<T>(k0);
-      op[ob + e1 * o.stride[3]] = from_f<T>(k1);
+#pragma unroll
+  for (int j = 0; j < kPairIters; ++j) {
+    const int i = tid + j * kStepThreads;
+    if (i < R * half) {
+      const int r = i / half, m = i % half;
+      const int e0 = R > 1 ? m : 2 * m;
+      const int e1 = R > 1 ? m + half : 2 * m + 1;
+      float a0 = q0[j], a1 = q1[j], c0 = k0[j], c1 = k1[j];
+      // SISO rotates pairs m < S; MIMO rotates (m, m + 2S) for m < S, and 2S == N/2 there.
+      if (m < S) {
+        const float cs = s_cos[m], sn = s_sin[m];
+        const float nq0 = rnd<T>(rnd<T>(a0 * cs) - rnd<T>(a1 * sn));
+        const float nq1 = rnd<T>(rnd<T>(a0 * sn) + rnd<T>(a1 * cs));
+        const float nk0 = rnd<T>(rnd<T>(c0 * cs) - rnd<T>(c1 * sn));
+        const float nk1 = rnd<T>(rnd<T>(c0 * sn) + rnd<T>(c1 * cs));
+        a0 = nq0; a1 = nq1; c0 = nk0; c1 = nk1;
+      }
+      s_q[r * N + e0] = a0;
+      s_q[r * N + e1] = a1;
+      s_k[r * N + e0] = c0;
+      s_k[r * N + e1] = c1;
+      if (write_small) {
+        const m3_tensor& o = a.out_k;
+        T* op = static_cast<T*>(o.data);
+        const int64_t ob = b * o.stride[0] + h * o.stride[1] + r * o.stride[2];
+        op[ob + e0 * o.stride[3]] = from_f<T>(c0);
+        op[ob + e1 * o.stride[3]] = from_f<T>(c1);
+      }
     }
   }
-  for (int i = tid; i < R * N; i += blockDim.x) {
-    const int r = i / N, n = i % N;
-    const m3_tensor& t = a.prev_k;
-    s_kp[i] = ld_t(t, b * t.stride[0] + h * t.stride[1] + r * t.stride[2] + n * t.stride[3]);
-  }
-  const float alpha = expf(ld_t(a.adt, b * a.adt.stride[0] + h * a.adt.stride[1]));
-  const float sg = sigmoidf_(ld_t(a.trap, b * a.trap.stride[0] + h * a.trap.stride[1]));
+  const float alpha = expf(adtv);
+  const float sg = sigmoidf_(trapv);
   const float beta = (1.0f - sg) * dtv * alpha;
   const float gamma = sg * dtv;
-  const float Dh = ld_t(a.D, h * a.D.stride[0]);
   __syncthreads();
+  return StepScalars{alpha, beta, gamma, Dh};
+}
+
+template <typename T, int R, int NPL>
+__global__ void __launch_bounds__(kStepThreads) step_kernel(const m3_step_args a, int rows_per_cta) {
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int p0 = blockIdx.x * rows_per_cta;
+  const int N = a.d_state, P = a.head_dim;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  extern __shared__ float sm[];
+  const float* s_q = sm + 128;
+  const float* s_k = s_q + R * N;
+  const float* s_kp = s_k + R * N;
+  const StepScalars sc = step_prologue<T, R>(a, b, h, blockIdx.x == 0, sm);
+  const float alpha = sc.alpha, beta = sc.beta, gamma = sc.gamma, Dh = sc.Dh;
 
   const float* st = static_cast<const float*>(a.state.data);
   float* so = static_cast<float*>(a.out_state.data);
@@ -176,9 +236,308 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const m3_step_args a
   }
 }
 
+
+// The state is touched exactly once per step: stream it past the caches.
+__device__ __forceinline__ float4 load_state4(const float* p) {
+#ifdef M3_STEP_STREAMING
+  return __ldcs(reinterpret_cast<const float4*>(p));
+#else
+  return *reinterpret_cast<const float4*>(p);
+#endif
+}
+__device__ __forceinline__ void store_state4(float* p, float4 v) {
+#ifdef M3_STEP_STREAMING
+  __stcs(reinterpret_cast<float4*>(p), v);
+#else
+  *reinterpret_cast<float4*>(p) = v;
+#endif
+}
+
+// Two-pass decode for state rows that are contiguous and 16-byte aligned.
+//
+// Pass 1 (step_prep_kernel, one CTA per (batch, head)): phase advance, rotation of q/k, the new
+// phase and rotated-k cache outputs, and the decay scalars, into the workspace:
+//   ws[(b H + h) W + ...], W = 2 R N + 4: rotated q [R][N], rotated k [R][N], then alpha, beta,
+//   gamma, D.
+// Pass 2 (step_stream_kernel): a pure stream over the FP32 state. Lane l of a warp holds the
+// float4 groups n = 4 l + 128 v (v < NV); every state row of the CTA, the per-head vectors and the
+// per-row inputs are loaded before any arithmetic, so each CTA has all of its HBM reads in flight
+// at once; each warp owns RPW consecutive rows.
+// One warp per (batch, head); four per CTA. Lane l owns angles l, l + 32 and rotation pairs
+// i = l + 32 j; the cos/sin of a pair's angle comes from its owner lane by shuffle.
+template <typename T, int R, int NT>
+__global__ void __launch_bounds__(kStepThreads) step_prep_kernel(const m3_step_args a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * (kStepThreads / 32) + (threadIdx.x >> 5);
+  if (wid >= (int64_t)a.batch * a.heads) return;
+  const int b = (int)(wid / a.heads), h = (int)(wid % a.heads);
+  // NT: d_state known at compile time (0 = read it from the arguments).
+  const int N = NT ? NT : a.d_state, S = a.num_angles, half = N / 2;
+  float* ws = static_cast<float*>(a.workspace.data) + wid * (2 * R * N + 4);
+  const T* qp = static_cast<const T*>(a.q.data);
+  const T* kp = static_cast<const T*>(a.k.data);
+
+  const float dtv = ld_t(a.dt, b * a.dt.stride[0] + h * a.dt.stride[1]);
+  const float adtv = ld_t(a.adt, b * a.adt.stride[0] + h * a.adt.stride[1]);
+  const float trapv = ld_t(a.trap, b * a.trap.stride[0] + h * a.trap.stride[1]);
+  const float Dh = ld_t(a.D, h * a.D.stride[0]);
+  float th[2] = {0.f, 0.f}, old[2] = {0.f, 0.f};
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int sidx = lane + 32 * u;
+    if (sidx < S) {
+      th[u] = ld_t(a.angle_rate, b * a.angle_rate.stride[0] + sidx * a.angle_rate.stride[1]);
+      old[u] = ld_t(a.phase, b * a.phase.stride[0] + h * a.phase.stride[1] + sidx * a.phase.stride[2]);
+    }
+  }
+  // Rotation pairs (e0, e1): SISO (2m, 2m+1), MIMO (m, m + N/2); processed 4 pairs per lane at a time
+  // so that the loads of a batch are in flight together.
+  const int npairs = R * half;
+  float cs[2] = {1.f, 1.f}, sn[2] = {0.f, 0.f};
+  for (int base = 0; base < npairs; base += 128) {
+    float q0[4], q1[4], k0[4], k1[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + lane + 32 * u;
+      q0[u] = q1[u] = k0[u] = k1[u] = 0.f;
+      if (i < npairs) {
+        const int r = i / half, m = i % half;
+        const int e0 = R > 1 ? m : 2 * m, e1 = R > 1 ? m + half : 2 * m + 1;
+        const int64_t qb = b * a.q.stride[0] + h * a.q.stride[1] + r * a.q.stride[2];
+        const int64_t kb = b * a.k.stride[0] + h * a.k.stride[1] + r * a.k.stride[2];
+        q0[u] = to_f(qp[qb + e0 * a.q.stride[3]]);
+        q1[u] = to_f(qp[qb + e1 * a.q.stride[3]]);
+        k0[u] = to_f(kp[kb + e0 * a.k.stride[3]]);
+        k1[u] = to_f(kp[kb + e1 * a.k.stride[3]]);
+        if (a.q_bias.data) {
+          const m3_tensor& qb_ = a.q_bias;
+          const m3_tensor& kb_ = a.k_bias;
+          const int64_t qo = h * qb_.stride[0] + r * qb_.stride[1];
+          const int64_t ko = h * kb_.stride[0] + r * kb_.stride[1];
+          q0[u] = rnd<T>(q0[u] + rnd<T>(ld_t(qb_, qo + e0 * qb_.stride[2])));
+          q1[u] = rnd<T>(q1[u] + rnd<T>(ld_t(qb_, qo + e1 * qb_.stride[2])));
+          k0[u] = rnd<T>(k0[u] + rnd<T>(ld_t(kb_, ko + e0 * kb_.stride[2])));
+          k1[u] = rnd<T>(k1[u] + rnd<T>(ld_t(kb_, ko + e1 * kb_.stride[2])));
+        }
+      }
+    }
+    if (base == 0) {
+      // New phase (computed while the first batch of q/k loads is in flight).
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int sidx = lane + 32 * u;
+        if (sidx < S) {
+          const float inc = fmodf((kPi * tanhf(th[u])) * dtv, kTwoPi);
+          const float ph = fmodf(old[u] + inc, kTwoPi);
+          const m3_tensor& o = a.out_phase;
+          static_cast<float*>(o.data)[b * o.stride[0] + h * o.stride[1] + sidx * o.stride[2]] = ph;
+          float s_, c_;
+          __sincosf(ph, &s_, &c_);  // |ph| < 2 pi: absolute error ~1e-6
+          cs[u] = rnd<T>(c_);
+          sn[u] = rnd<T>(s_);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + lane + 32 * u;
+      const int m = (i < npairs) ? i % half : 0;
+      // cos/sin of angle m live in lane m % 32, slot m / 32 (every lane joins the shuffles).
+      const float c0 = __shfl_sync(0xffffffffu, cs[0], m & 31), c1 = __shfl_sync(0xffffffffu, cs[1], m & 31);
+      const float s0 = __shfl_sync(0xffffffffu, sn[0], m & 31), s1 = __shfl_sync(0xffffffffu, sn[1], m & 31);
+      if (i < npairs) {
+        const int r = i / half;
+        const int e0 = R > 1 ? m : 2 * m, e1 = R > 1 ? m + half : 2 * m + 1;
+        float a0 = q0[u], a1 = q1[u], b0 = k0[u], b1 = k1[u];
+        // SISO rotates pairs m < S; MIMO rotates (m, m + 2S) for m < S, and 2S == N/2 there.
+        if (m < S) {
+          const float c = (m < 32) ? c0 : c1, sv = (m < 32) ? s0 : s1;
+          const float nq0 = rnd<T>(rnd<T>(a0 * c) - rnd<T>(a1 * sv));
+          const float nq1 = rnd<T>(rnd<T>(a0 * sv) + rnd<T>(a1 * c));
+          const float nk0 = rnd<T>(rnd<T>(b0 * c) - rnd<T>(b1 * sv));
+          const float nk1 = rnd<T>(rnd<T>(b0 * sv) + rnd<T>(b1 * c));
+          a0 = nq0; a1 = nq1; b0 = nk0; b1 = nk1;
+        }
+        ws[r * N + e0] = a0;
+        ws[r * N + e1] = a1;
+        ws[R * N + r * N + e0] = b0;
+        ws[R * N + r * N + e1] = b1;
+        const m3_tensor& o = a.out_k;
+        T* op = static_cast<T*>(o.data);
+        const int64_t ob = b * o.stride[0] + h * o.stride[1] + r * o.stride[2];
+        op[ob + e0 * o.stride[3]] = from_f<T>(b0);
+        op[ob + e1 * o.stride[3]] = from_f<T>(b1);
+      }
+    }
+  }
+  if (lane == 0) {
+    const float alpha = expf(adtv);
+    const float sg = sigmoidf_(trapv);
+    *reinterpret_cast<float4*>(ws + 2 * R * N) = make_float4(alpha, (1.0f - sg) * dtv * alpha, sg * dtv, Dh);
+  }
+}
+
+template <typename T, int R, int NV, int RPW>
+__global__ void __launch_bounds__(kStepThreads) step_stream_kernel(const m3_step_args a, int vec_prev_k) {
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int N = a.d_state, P = a.head_dim;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int p0 = blockIdx.x * (RPW * (kStepThreads / 32)) + warp * RPW;
+  const float* st = static_cast<const float*>(a.state.data) + b * a.state.stride[0] + h * a.state.stride[1];
+  float* so = static_cast<float*>(a.out_state.data) + b * a.out_state.stride[0] + h * a.out_state.stride[1];
+  const float* ws = static_cast<const float*>(a.workspace.data) + ((int64_t)b * a.heads + h) * (2 * R * N + 4);
+  float4 sv[RPW][NV];
+#pragma unroll
+  for (int rr = 0; rr < RPW; ++rr) {
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int n = 4 * lane + 128 * v, p = p0 + rr;
+      sv[rr][v] = (p < P && n < N) ? load_state4(st + p * a.state.stride[2] + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  float4 qv[R][NV], kv[R][NV], kpv[R][NV];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int n = 4 * lane + 128 * v;
+      qv[r][v] = kv[r][v] = kpv[r][v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (n < N) {
+        qv[r][v] = *reinterpret_cast<const float4*>(ws + r * N + n);
+        kv[r][v] = *reinterpret_cast<const float4*>(ws + R * N + r * N + n);
+        const m3_tensor& t = a.prev_k;
+        const int64_t kb = b * t.stride[0] + h * t.stride[1] + r * t.stride[2];
+        if (vec_prev_k) {  // four packed 16-bit values
+          const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const T*>(t.data) + kb + n);
+          const T* e = reinterpret_cast<const T*>(&w);
+          kpv[r][v] = make_float4(to_f(e[0]), to_f(e[1]), to_f(e[2]), to_f(e[3]));
+        } else {
+          kpv[r][v] = make_float4(ld_t(t, kb + n * t.stride[3]), ld_t(t, kb + (n + 1) * t.stride[3]),
+                                  ld_t(t, kb + (n + 2) * t.stride[3]), ld_t(t, kb + (n + 3) * t.stride[3]));
+        }
+      }
+    }
+  }
+  const float4 sc = *reinterpret_cast<const float4*>(ws + 2 * R * N);  // alpha, beta, gamma, D
+  // Per-row inputs: lane rr of the warp loads row p0 + rr.
+  float x_l = 0.f, xp_l = 0.f, z_l = 0.f;
+  if (lane < RPW && p0 + lane < P) {
+    const int p = p0 + lane;
+    x_l = ld_t(a.value, b * a.value.stride[0] + h * a.value.stride[1] + p * a.value.stride[2]);
+    xp_l = ld_t(a.prev_value, b * a.prev_value.stride[0] + h * a.prev_value.stride[1] + p * a.prev_value.stride[2]);
+    z_l = ld_t(a.gate, b * a.gate.stride[0] + h * a.gate.stride[1] + p * a.gate.stride[2]);
+  }
+  float acc_l[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc_l[r] = 0.0f;
+#pragma unroll
+  for (int rr = 0; rr < RPW; ++rr) {
+    const int p = p0 + rr;
+    if (p >= P) break;  // warp-uniform
+    const float x = __shfl_sync(0xffffffffu, x_l, rr), xp = __shfl_sync(0xffffffffu, xp_l, rr);
+    float xv[R], xpv[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (R > 1) {
+        const float mx = rnd<T>(ld_t(a.mimo_x, h * a.mimo_x.stride[0] + r * a.mimo_x.stride[1] + p * a.mimo_x.stride[2]));
+        xv[r] = rnd<T>(x * mx);
+        xpv[r] = rnd<T>(xp * mx);
+      } else {
+        xv[r] = x;
+        xpv[r] = xp;
+      }
+    }
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int n = 4 * lane + 128 * v;
+      if (n < N) {
+        float4 po = make_float4(0.f, 0.f, 0.f, 0.f), co = po;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          po.x += xpv[r] * kpv[r][v].x; po.y += xpv[r] * kpv[r][v].y;
+          po.z += xpv[r] * kpv[r][v].z; po.w += xpv[r] * kpv[r][v].w;
+          co.x += xv[r] * kv[r][v].x; co.y += xv[r] * kv[r][v].y;
+          co.z += xv[r] * kv[r][v].z; co.w += xv[r] * kv[r][v].w;
+        }
+        const float4 o = sv[rr][v];
+        float4 ns;
+        ns.x = sc.x * o.x + sc.y * po.x + sc.z * co.x;
+        ns.y = sc.x * o.y + sc.y * po.y + sc.z * co.y;
+        ns.z = sc.x * o.z + sc.y * po.z + sc.z * co.z;
+        ns.w = sc.x * o.w + sc.y * po.w + sc.z * co.w;
+        store_state4(so + p * a.out_state.stride[2] + n, ns);
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          acc[r] += rnd<T>(ns.x) * qv[r][v].x + rnd<T>(ns.y) * qv[r][v].y + rnd<T>(ns.z) * qv[r][v].z +
+                    rnd<T>(ns.w) * qv[r][v].w;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      acc[r] = warp_sum(acc[r]);
+      if (lane == rr) acc_l[r] = acc[r];  // lane rr finishes row rr below
+    }
+  }
+  // Row epilogues, one row per lane: y = sum_r mo_r silu(z mz_r) (S' q_r + D x mx_r).
+  if (lane < RPW && p0 + lane < P) {
+    const int p = p0 + lane;
+    float y = 0.0f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float xr = x_l, zr = z_l;
+      if (R > 1) {
+        xr = rnd<T>(x_l * rnd<T>(ld_t(a.mimo_x, h * a.mimo_x.stride[0] + r * a.mimo_x.stride[1] + p * a.mimo_x.stride[2])));
+        zr = rnd<T>(z_l * rnd<T>(ld_t(a.mimo_z, h * a.mimo_z.stride[0] + r * a.mimo_z.stride[1] + p * a.mimo_z.stride[2])));
+      }
+      float o = (acc_l[r] + sc.w * xr) * __fdividef(zr, 1.0f + __expf(-zr));
+      if (R > 1) o *= ld_t(a.mimo_out, h * a.mimo_out.stride[0] + r * a.mimo_out.stride[1] + p * a.mimo_out.stride[2]);
+      y += o;
+    }
+    static_cast<T*>(a.y.data)[b * a.y.stride[0] + h * a.y.stride[1] + p * a.y.stride[2]] = from_f<T>(y);
+  }
+}
+
+template <typename T, int R, int NV, int RPW>
+static cudaError_t launch_step_two_pass(const m3_step_args& a, cudaStream_t stream) {
+  const int64_t pairs = (int64_t)a.batch * a.heads;
+  const int per_cta = kStepThreads / 32;
+  const unsigned grid = (unsigned)((pairs + per_cta - 1) / per_cta);
+  if (a.d_state == 128) step_prep_kernel<T, R, 128><<<grid, kStepThreads, 0, stream>>>(a);
+  else step_prep_kernel<T, R, 0><<<grid, kStepThreads, 0, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int rows = RPW * (kStepThreads / 32);
+  const m3_tensor& pk = a.prev_k;
+  const int vec_prev_k = sizeof(T) == 2 && pk.stride[3] == 1 && (reinterpret_cast<uintptr_t>(pk.data) & 7u) == 0 &&
+                         pk.stride[0] % 4 == 0 && pk.stride[1] % 4 == 0 && pk.stride[2] % 4 == 0;
+  step_stream_kernel<T, R, NV, RPW><<<dim3((a.head_dim + rows - 1) / rows, a.heads, a.batch), kStepThreads, 0,
+                                      stream>>>(a, vec_prev_k);
+  return cudaGetLastError();
+}
+
+bool step_vec_ok(const m3_step_args& a) {
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const m3_tensor& s = a.state;
+  const m3_tensor& o = a.out_state;
+  return a.d_state % 4 == 0 && a.d_state <= 256 && s.stride[3] == 1 && o.stride[3] == 1 && al16(s.data) &&
+         al16(o.data) && s.stride[0] % 4 == 0 && s.stride[1] % 4 == 0 && s.stride[2] % 4 == 0 &&
+         o.stride[0] % 4 == 0 && o.stride[1] % 4 == 0 && o.stride[2] % 4 == 0;
+}
+
 template <typename T, int R>
 static cudaError_t launch_step_r(const m3_step_args& a, cudaStream_t stream) {
   const int N = a.d_state, P = a.head_dim;
+  if (a.workspace.data != nullptr) {  // set exactly when step_vec_ok (m3_step_workspace_bytes)
+    // kStepBigRows rows per warp once there are enough (batch, head) pairs to fill
+    // the GPU several times; otherwise 2 rows per warp so that even batch 1 spreads over all SMs.
+    const bool big = (long long)a.batch * a.heads >= 4 * 148;
+    if (N <= 128)
+      return big ? launch_step_two_pass<T, R, 1, kStepBigRows>(a, stream) : launch_step_two_pass<T, R, 1, 2>(a, stream);
+    return big ? launch_step_two_pass<T, R, 2, 8>(a, stream) : launch_step_two_pass<T, R, 2, 2>(a, stream);
+  }
   // Split rows across CTAs until the grid covers every SM a few times.
   int rows = P;
   const long long pairs = (long long)a.batch * a.heads;
@@ -207,6 +566,11 @@ static cudaError_t launch_step_t(const m3_step_args& a, cudaStream_t stream) {
     case 4: return launch_step_r<T, 4>(a, stream);
     default: return launch_step_r<T, 8>(a, stream);
   }
+}
+
+int64_t step_workspace_bytes(const m3_step_args& a) {
+  if (!step_vec_ok(a)) return 0;
+  return (int64_t)a.batch * a.heads * (2 * a.rank * a.d_state + 4) * (int64_t)sizeof(float);
 }
 
 cudaError_t launch_step(const m3_step_args& a, cudaStream_t stream) {
