@@ -69,8 +69,14 @@ def test_noalloc_rejects_sizes_beyond_the_fixed_scratch():
     args = _ext.ScanArgs()
     args.batch, args.length, args.groups, args.heads, args.rank = 64, 100_000, 1, 2, 1
     args.d_state, args.head_dim, args.num_angles, args.chunk_hint, args.device = 128, 64, 32, 256, 0
-    args.value = _ext.M3Tensor(data=1, dtype=_ext.M3_BF16, ndim=4)
-    args.q_norm_w = _ext.M3Tensor(data=1, dtype=_ext.M3_F32, ndim=1)
+    # Descriptors only (nothing is launched): aligned, contiguous-row layouts of the shapes above.
+    def desc(nd, dtype=_ext.M3_BF16):
+        t = _ext.M3Tensor(data=256, dtype=dtype, ndim=nd)
+        for i in range(nd):
+            t.stride[i] = 1 if i == nd - 1 else 1024
+        return t
+    args.q, args.k, args.value, args.gate = desc(5), desc(5), desc(4), desc(4)
+    args.q_norm_w = desc(1, _ext.M3_F32)
     assert lib.m3_scan_workspace_bytes(ctypes.byref(args)) > 8 * 1024 * 1024
     assert lib.m3_scan_fwd_noalloc(ctypes.byref(args), None) == 1  # M3_ERR_SHAPE, nothing launched
     assert b"fixed limit" in lib.m3_last_error()
