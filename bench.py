@@ -178,6 +178,9 @@ def scan_flops_per_token_layer(model, chunk) -> float:
 def run_prefill(args, world, rank, local):
     from mamba3_b200 import _ext, ops
     d_model, depth, mrank, causal, batch, length = WORKLOADS[args.workload]
+    batch = args.batch or batch
+    length = args.seq_len or length
+    depth = args.depth or depth
     model = build_model(d_model, depth, mrank, causal)
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     x = torch.randn(batch, length, d_model, device="cuda", generator=g)
@@ -222,7 +225,8 @@ def run_prefill(args, world, rank, local):
     flops_launch = scan_flops_per_token_layer(model, 128 // mrank if mrank > 1 else 128) * batch * length
     achieved = bytes_launch / (kernel_ms / 1e3) / 1e9
     tflops = flops_launch / (kernel_ms / 1e3) / 1e12
-    launches_per_step = depth * (1 if causal else 2)
+    # per layer and direction: the token pre-pass and the chunked-SSD kernel
+    launches_per_step = depth * 2 * (1 if causal else 2)
     result = {
         "metric": "prefill_tokens_per_s",
         "value": value,
@@ -258,10 +262,12 @@ def run_prefill(args, world, rank, local):
 def run_decode(args, world, rank):
     """CUDA-graph decode step of Mamba3(2560, depth=32) at batch 64 (bf16 params, FP32 state)."""
     from mamba3_b200 import ops
-    model = build_model(DECODE["d_model"], DECODE["depth"], 1, True).to(torch.bfloat16)
-    decoder = model.cuda_graph(batch_size=DECODE["batch"])
+    batch = (args.batch if args.only == "decode" and args.batch else DECODE["batch"])
+    depth = (args.depth if args.only == "decode" and args.depth else DECODE["depth"])
+    model = build_model(DECODE["d_model"], depth, 1, True).to(torch.bfloat16)
+    decoder = model.cuda_graph(batch_size=batch)
     g = torch.Generator(device="cuda").manual_seed(99 + rank)
-    xs = torch.randn(16, DECODE["batch"], 1, DECODE["d_model"], device="cuda", dtype=torch.bfloat16, generator=g)
+    xs = torch.randn(16, batch, 1, DECODE["d_model"], device="cuda", dtype=torch.bfloat16, generator=g)
     for i in range(5):
         decoder(xs[i % 16])
     n = max(args.steps * 10, 50)
@@ -269,7 +275,7 @@ def run_decode(args, world, rank):
     us = timed(lambda: decoder(xs[next(it) % 16]), n, world) * 1e3
     # step-kernel roofline: one layer's step kernel alone, in place (as in the graph)
     mixer = model.layers[0].mixer
-    cache = mixer.allocate_cache(DECODE["batch"], device="cuda", dtype=torch.bfloat16)
+    cache = mixer.allocate_cache(batch, device="cuda", dtype=torch.bfloat16)
     with torch.inference_mode():
         q, k, xv, z, adt, dt, trap, ang = mixer._project(mixer_input := model.layers[0].norm(xs[0]))
         qh = q[:, 0].expand(-1, mixer.nheads, -1, -1)
@@ -284,8 +290,8 @@ def run_decode(args, world, rank):
         kus = timed(kern, 50, world) * 1e3
     del mixer_input
     pk, _ = peaks()
-    state_bytes = 2 * DECODE["batch"] * mixer.nheads * mixer.headdim * mixer.d_state * 4
-    return {"us_per_step": us, "batch": DECODE["batch"], "model": "Mamba3(2560, depth=32, mimo_rank=1) bf16",
+    state_bytes = 2 * batch * mixer.nheads * mixer.headdim * mixer.d_state * 4
+    return {"us_per_step": us, "batch": batch, "model": f"Mamba3(2560, depth={depth}, mimo_rank=1) bf16",
             "step_kernel_us": kus, "step_kernel_state_gbs": state_bytes / (kus / 1e6) / 1e9,
             "step_kernel_frac": state_bytes / (kus / 1e6) / 1e9 / pk["hbm_gbs"],
             "state_bytes_per_layer": state_bytes}
@@ -322,6 +328,11 @@ def main():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="siso")
     p.add_argument("--no-decode", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--only", choices=["prefill", "decode"], default=None,
+                   help="run one part (profiling); the default run measures both")
+    p.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling cases)")
+    p.add_argument("--seq-len", type=int, default=0, help="override the sequence length (profiling cases)")
+    p.add_argument("--depth", type=int, default=0, help="override the depth (profiling cases)")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
 
@@ -347,10 +358,13 @@ def main():
         return
 
     world, rank, local = dist_setup()
-    result = run_prefill(args, world, rank, local)
-    if not args.no_decode:
-        result["decode"] = run_decode(args, world, rank)
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if args.only == "decode":
+        result = {"decode": run_decode(args, world, rank)}
+    else:
+        result = run_prefill(args, world, rank, local)
+        if not args.no_decode and args.only != "prefill":
+            result["decode"] = run_decode(args, world, rank)
+    if rank == 0 and world == 1 and not args.no_cpu and args.only is None:
         result["cpu_baseline"] = cpu_baseline(args)
     if rank == 0:
         print(json.dumps(result))

@@ -1,0 +1,44 @@
+"""Batch sharding of Mamba3 over one process per GPU.
+
+Every (sequence, head) scan is independent, so the sequences of a batch split across ranks with no
+exchange during the layers: each rank runs the whole model on its contiguous slice of the batch and
+one all-gather at the end assembles the full output (over NCCL/NVLink on GPUs; gloo in CPU tests).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def shard_bounds(batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous near-equal split: the first ``batch % world`` ranks get one extra sequence."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    base, extra = divmod(batch, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def forward_sharded(model, x: torch.Tensor, group=None) -> torch.Tensor:
+    """Run ``model`` on this rank's share of the batch of ``x`` and all-gather the full output.
+
+    ``x`` is the full batch (every rank passes the same tensor, or at least the same shape); the
+    result is the full ``model(x)`` on every rank. Ranks with an empty share still take part in
+    the gather.
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    batch = x.shape[0]
+    start, stop = shard_bounds(batch, world, rank)
+    local = model(x[start:stop]) if stop > start else x[:0].new_empty((0, *x.shape[1:]))
+    widest = -(-batch // world)
+    padded = local.new_zeros((widest, *local.shape[1:]))
+    padded[: local.shape[0]] = local
+    parts = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(parts, padded.contiguous(), group=group)
+    pieces = []
+    for r, part in enumerate(parts):
+        s, e = shard_bounds(batch, world, r)
+        pieces.append(part[: e - s])
+    return torch.cat(pieces, dim=0)
