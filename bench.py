@@ -41,6 +41,10 @@ WORKLOADS = {
     "bidir": (768, 12, 1, False, 32, 2048),
 }
 DECODE = dict(d_model=2560, depth=32, batch=64)
+# DRAM bytes (read + write) per token of one scan-kernel launch, from one ncu capture of the same
+# kernel on a smaller case of the workload (dram__bytes_read.sum + dram__bytes_write.sum = 192.33 MB
+# over 2 x 8192 tokens, d_model 1024, rank 1). Traffic grows with tokens, so the bench scales it.
+SCAN_TRAFFIC_PER_TOKEN = {"siso": 192.33e6 / 16384}
 
 
 def peaks() -> tuple[dict, str]:
@@ -251,7 +255,10 @@ def run_prefill(args, world, rank, local):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_kind": pk_kind,
+                     "frac": achieved / pk["hbm_gbs"],
+                     "traffic": (SCAN_TRAFFIC_PER_TOKEN[args.workload] * batch * length
+                                 if args.workload in SCAN_TRAFFIC_PER_TOKEN and mrank == 1 and d_model == 1024
+                                 else None), "peak_kind": pk_kind,
                      "kernel": f"m3 scan ({kernel_name})", "kernel_ms": kernel_ms,
                      "algorithmic_bytes_per_launch": bytes_launch,
                      "tensor_tflops": tflops, "tensor_frac": tflops / pk["bf16_tflops"]},

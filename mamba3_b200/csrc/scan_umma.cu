@@ -430,10 +430,10 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
   // Workspace rows (cp.async) or their stand-ins, and the phase tensor of the op-level API.
   auto fetch_small = [&](int t0n, int ntn) {
     if (has_ws) {
-      const int chunks = WS / 4;
-      for (int c = tid; c < TOK * chunks; c += kThreads) {
-        const int j = c / chunks, c4 = c % chunks;
-        if (j < ntn) {
+      const int chunks = WS / 4;  // <= 12: one 16-slot row per token, no division
+      for (int c = tid; c < TOK * 16; c += kThreads) {
+        const int j = c >> 4, c4 = c & 15;
+        if (j < ntn && c4 < chunks) {
           const int t = scan_token(a, t0n + j);
           cp_async16(smem_u32(wsb + j * WS + 4 * c4), ws + ws_b + (int64_t)t * WS + 4 * c4);
         }
@@ -853,8 +853,10 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
       fetch_small(t0n, ntn);
       issue_z(t0n, ntn, (tile + 1) & 1);
     }
-    if (!mbar_wait(bar_addr, phase_bit)) *abort_flag = 1;
+    // One thread polls the barrier; the others wait at __syncthreads without taking issue slots.
+    if (tid == 0 && !mbar_wait(bar_addr, phase_bit)) *abort_flag = 1;
     phase_bit ^= 1;
+    __syncthreads();
     fence_after();
     // Q'/K' are free now: the next tile's raw q/k rows.
     if (ntn > 0) issue_qk(t0n, ntn);
@@ -918,8 +920,9 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
       }
       mma_commit(bar_addr);
     }
-    if (!mbar_wait(bar_addr, phase_bit)) *abort_flag = 1;
+    if (tid == 0 && !mbar_wait(bar_addr, phase_bit)) *abort_flag = 1;
     phase_bit ^= 1;
+    __syncthreads();
     fence_after();
     // W is free now: the next tile's raw x rows.
     if (ntn > 0) issue_x(t0n, ntn);
