@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define M3_ABI_VERSION 1
+#define M3_ABI_VERSION 2
 
 enum m3_dtype { M3_F32 = 0, M3_F16 = 1, M3_BF16 = 2 };
 
@@ -116,16 +116,23 @@ typedef struct m3_scan_args {
  *   workspace   float32 scratch of m3_step_workspace_bytes(args) bytes (contiguous), required
  *               when that size is non-zero: the per-(batch, head) rotated q/k and decay scalars
  *               a pre-pass computes so that the state pass is a pure stream over HBM
+ * Model mode (the projection post-processing of mamba3/model.py:189-199 done in the kernel):
+ *   q_norm_w, k_norm_w [N]  optional, together: q/k are the raw C/B rows of the projection and
+ *               are RMS-normalised (epsilon norm_eps) with these weights before the bias
+ *   dt_bias [H] optional: dt holds the raw delta logits and adt the raw decay logits (any float
+ *               dtype); the kernel forms dt = softplus(delta + dt_bias) and
+ *               adt = min(-heavy_tail(decay), -1e-4) * dt
  */
 typedef struct m3_step_args {
   int32_t batch, heads, rank, d_state, head_dim, num_angles;
   int32_t device;         /* CUDA device ordinal of every tensor and of `stream` (-1: current) */
-  int32_t reserved;
+  float norm_eps;         /* RMS-norm epsilon for q_norm_w / k_norm_w */
   m3_tensor q, k, q_bias, k_bias, value, gate;
   m3_tensor adt, dt, trap, angle_rate, D, mimo_x, mimo_z, mimo_out;
   m3_tensor phase, state, prev_k, prev_value;
   m3_tensor y, out_phase, out_state, out_k;
   m3_tensor workspace;
+  m3_tensor q_norm_w, k_norm_w, dt_bias;
 } m3_step_args;
 
 /* Chunked SSD forward. Returns M3_OK or an M3_ERR_* code. */

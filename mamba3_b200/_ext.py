@@ -17,7 +17,7 @@ _LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmamba3_b200.so"
 
 M3_F32, M3_F16, M3_BF16 = 0, 1, 2
 _DTYPES = {torch.float32: M3_F32, torch.float16: M3_F16, torch.bfloat16: M3_BF16}
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class M3Tensor(ctypes.Structure):
@@ -46,6 +46,7 @@ _STEP_TENSORS = (
     "phase", "state", "prev_k", "prev_value",
     "y", "out_phase", "out_state", "out_k",
     "workspace",
+    "q_norm_w", "k_norm_w", "dt_bias",
 )
 
 
@@ -59,7 +60,8 @@ class ScanArgs(ctypes.Structure):
 
 class StepArgs(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in (
-        "batch", "heads", "rank", "d_state", "head_dim", "num_angles", "device", "reserved")] + [
+        "batch", "heads", "rank", "d_state", "head_dim", "num_angles", "device")] + [
+        ("norm_eps", ctypes.c_float)] + [
         (name, M3Tensor) for name in _STEP_TENSORS]
 
 
@@ -165,12 +167,13 @@ def scan_forward(*, sizes: dict, tensors: dict, reverse: bool = False, mimo_rota
 
 
 @torch.compiler.disable
-def step_forward(*, sizes: dict, tensors: dict) -> None:
+def step_forward(*, sizes: dict, tensors: dict, norm_eps: float = 1e-5) -> None:
     """Enqueue ``m3_step_fwd`` on the current stream of the tensors' device."""
     lib = load()
     args = StepArgs()
     for key, val in sizes.items():
         setattr(args, key, int(val))
+    args.norm_eps = float(norm_eps)
     device = _cuda_device(tensors)
     args.device = device.index if device.index is not None else torch.cuda.current_device()
     for name in _STEP_TENSORS:

@@ -99,19 +99,26 @@ int m3_step_fwd(const m3_step_args* args, void* stream) {
       {&a.prev_k, "previous_k", 4, true}, {&a.prev_value, "previous_value", 3, true}, {&a.y, "output", 3, true},
       {&a.out_phase, "output_phase", 3, true}, {&a.out_state, "output_state", 4, true},
       {&a.out_k, "output_k", 4, true}, {&a.workspace, "workspace", 1, false},
+      {&a.q_norm_w, "q_norm_w", 1, false}, {&a.k_norm_w, "k_norm_w", 1, false}, {&a.dt_bias, "dt_bias", 1, false},
   };
   for (const Item& it : items) {
     const int rc = check_tensor(*it.t, it.name, it.nd, it.req);
     if (rc != M3_OK) return rc;
   }
   M3_REQUIRE(present(a.q_bias) == present(a.k_bias), M3_ERR_ARGUMENT, "q_bias and k_bias must be given together");
+  M3_REQUIRE(present(a.q_norm_w) == present(a.k_norm_w), M3_ERR_ARGUMENT,
+             "q_norm_w and k_norm_w must be given together");
+  M3_REQUIRE(!present(a.q_norm_w) || a.norm_eps > 0.0f, M3_ERR_ARGUMENT, "norm_eps must be positive");
+  const bool raw_dt = present(a.dt_bias);
   const int act = a.value.dtype;
   M3_REQUIRE(a.q.dtype == act && a.k.dtype == act && a.gate.dtype == act && a.y.dtype == act &&
                  a.out_k.dtype == act && a.prev_k.dtype == act && a.prev_value.dtype == act,
              M3_ERR_DTYPE, "q, k, value, gate, output and the K/value caches must share one dtype");
   M3_REQUIRE(a.phase.dtype == M3_F32 && a.state.dtype == M3_F32 && a.out_phase.dtype == M3_F32 &&
-                 a.out_state.dtype == M3_F32 && a.adt.dtype == M3_F32 && a.dt.dtype == M3_F32,
-             M3_ERR_DTYPE, "phase, state, adt and dt must be float32");
+                 a.out_state.dtype == M3_F32,
+             M3_ERR_DTYPE, "phase and state must be float32");
+  M3_REQUIRE(raw_dt || (a.adt.dtype == M3_F32 && a.dt.dtype == M3_F32), M3_ERR_DTYPE,
+             "adt and dt must be float32 unless dt_bias is given");
   M3_REQUIRE(a.rank > 1 || !present(a.mimo_x), M3_ERR_ARGUMENT, "MIMO projections require rank > 1");
   M3_REQUIRE(a.out_phase.data != a.phase.data && a.out_k.data != a.prev_k.data, M3_ERR_LAYOUT,
              "output phase / k must not alias the input cache");

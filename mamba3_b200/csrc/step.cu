@@ -29,6 +29,39 @@ struct StepScalars {
   float alpha, beta, gamma, Dh;
 };
 
+// dt and adt of (b, h). Model mode (dt_bias given, mamba3/model.py:195-198): dt holds the raw
+// delta logits and adt the raw decay logits; dt = softplus(delta + dt_bias),
+// adt = min(-heavy_tail(decay), -1e-4) * dt. Otherwise both are taken as given.
+__device__ __forceinline__ void step_dt_adt(const m3_step_args& a, int b, int h, float& dtv, float& adtv) {
+  const float d = ld_t(a.dt, b * a.dt.stride[0] + h * a.dt.stride[1]);
+  const float g = ld_t(a.adt, b * a.adt.stride[0] + h * a.adt.stride[1]);
+  if (a.dt_bias.data) {
+    dtv = softplusf_(d + ld_t(a.dt_bias, h * a.dt_bias.stride[0]));
+    adtv = fminf(-heavy_tailf(g), -kAFloor) * dtv;
+  } else {
+    dtv = d;
+    adtv = g;
+  }
+}
+
+// Sum of squares of row r of a [B,H,R,N] tensor over one warp (every lane gets the total).
+template <typename T>
+__device__ __forceinline__ float row_sumsq(const m3_tensor& t, int b, int h, int r, int N, int lane) {
+  const T* p = static_cast<const T*>(t.data) + b * t.stride[0] + h * t.stride[1] + r * t.stride[2];
+  float acc = 0.0f;
+  for (int n = lane; n < N; n += 32) {
+    const float v = to_f(p[n * t.stride[3]]);
+    acc += v * v;
+  }
+  return warp_sum(acc);
+}
+
+// RMS-normalised element (F.rms_norm with the weight cast to the activation dtype, one rounding).
+template <typename T>
+__device__ __forceinline__ float norm_elem(float x, float inv_rms, const m3_tensor& w, int e) {
+  return rnd<T>(x * inv_rms * rnd<T>(ld_t(w, e * w.stride[0])));
+}
+
 template <typename T, int R>
 __device__ __forceinline__ StepScalars step_prologue(const m3_step_args& a, int b, int h, bool write_small, float* sm) {
   // Every global load of the prologue is issued first (one memory round trip), then the math.
@@ -42,11 +75,21 @@ __device__ __forceinline__ StepScalars step_prologue(const m3_step_args& a, int 
   float* s_q = sm + 128;        // R * N   rotated q (activation-rounded)
   float* s_k = s_q + R * N;     // R * N   rotated k
   float* s_kp = s_k + R * N;    // R * N   previous rotated k (cache)
+  float* s_rn = s_kp + R * N;   // 2 R     inverse RMS of the q rows, then of the k rows
   const T* qp = static_cast<const T*>(a.q.data);
   const T* kp = static_cast<const T*>(a.k.data);
+  const bool has_norm = a.q_norm_w.data != nullptr;
+  if (has_norm) {
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int j = warp; j < 2 * R; j += kStepThreads / 32) {
+      const float ss = row_sumsq<T>(j < R ? a.q : a.k, b, h, j % R, N, lane);
+      if (lane == 0) s_rn[j] = rsqrtf(ss / N + a.norm_eps);
+    }
+    __syncthreads();
+  }
 
-  const float dtv = ld_t(a.dt, b * a.dt.stride[0] + h * a.dt.stride[1]);
-  const float adtv = ld_t(a.adt, b * a.adt.stride[0] + h * a.adt.stride[1]);
+  float dtv, adtv;
+  step_dt_adt(a, b, h, dtv, adtv);
   const float trapv = ld_t(a.trap, b * a.trap.stride[0] + h * a.trap.stride[1]);
   const float Dh = ld_t(a.D, h * a.D.stride[0]);
   float th = 0.0f, old = 0.0f;
@@ -71,6 +114,12 @@ __device__ __forceinline__ StepScalars step_prologue(const m3_step_args& a, int 
       q1[j] = to_f(qp[qb + e1 * a.q.stride[3]]);
       k0[j] = to_f(kp[kb + e0 * a.k.stride[3]]);
       k1[j] = to_f(kp[kb + e1 * a.k.stride[3]]);
+      if (has_norm) {
+        q0[j] = norm_elem<T>(q0[j], s_rn[r], a.q_norm_w, e0);
+        q1[j] = norm_elem<T>(q1[j], s_rn[r], a.q_norm_w, e1);
+        k0[j] = norm_elem<T>(k0[j], s_rn[R + r], a.k_norm_w, e0);
+        k1[j] = norm_elem<T>(k1[j], s_rn[R + r], a.k_norm_w, e1);
+      }
       if (a.q_bias.data) {
         const m3_tensor& qb_ = a.q_bias;
         const m3_tensor& kb_ = a.k_bias;
@@ -277,10 +326,24 @@ __global__ void __launch_bounds__(kStepThreads) step_prep_kernel(const m3_step_a
   const T* qp = static_cast<const T*>(a.q.data);
   const T* kp = static_cast<const T*>(a.k.data);
 
-  const float dtv = ld_t(a.dt, b * a.dt.stride[0] + h * a.dt.stride[1]);
-  const float adtv = ld_t(a.adt, b * a.adt.stride[0] + h * a.adt.stride[1]);
+  float dtv, adtv;
+  step_dt_adt(a, b, h, dtv, adtv);
   const float trapv = ld_t(a.trap, b * a.trap.stride[0] + h * a.trap.stride[1]);
   const float Dh = ld_t(a.D, h * a.D.stride[0]);
+  // Model mode: inverse RMS of q row r and k row r live in lane r (fetched by shuffle).
+  const bool has_norm = a.q_norm_w.data != nullptr;
+  float my_rq = 1.0f, my_rk = 1.0f;
+  if (has_norm) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float sq = row_sumsq<T>(a.q, b, h, r, N, lane);
+      const float sk = row_sumsq<T>(a.k, b, h, r, N, lane);
+      if (lane == r) {
+        my_rq = rsqrtf(sq / N + a.norm_eps);
+        my_rk = rsqrtf(sk / N + a.norm_eps);
+      }
+    }
+  }
   float th[2] = {0.f, 0.f}, old[2] = {0.f, 0.f};
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
@@ -300,6 +363,8 @@ __global__ void __launch_bounds__(kStepThreads) step_prep_kernel(const m3_step_a
     for (int u = 0; u < 4; ++u) {
       const int i = base + lane + 32 * u;
       q0[u] = q1[u] = k0[u] = k1[u] = 0.f;
+      const int rr = (i < npairs ? i : npairs - 1) / half;
+      const float rq = __shfl_sync(0xffffffffu, my_rq, rr), rk = __shfl_sync(0xffffffffu, my_rk, rr);
       if (i < npairs) {
         const int r = i / half, m = i % half;
         const int e0 = R > 1 ? m : 2 * m, e1 = R > 1 ? m + half : 2 * m + 1;
@@ -309,6 +374,12 @@ __global__ void __launch_bounds__(kStepThreads) step_prep_kernel(const m3_step_a
         q1[u] = to_f(qp[qb + e1 * a.q.stride[3]]);
         k0[u] = to_f(kp[kb + e0 * a.k.stride[3]]);
         k1[u] = to_f(kp[kb + e1 * a.k.stride[3]]);
+        if (has_norm) {
+          q0[u] = norm_elem<T>(q0[u], rq, a.q_norm_w, e0);
+          q1[u] = norm_elem<T>(q1[u], rq, a.q_norm_w, e1);
+          k0[u] = norm_elem<T>(k0[u], rk, a.k_norm_w, e0);
+          k1[u] = norm_elem<T>(k1[u], rk, a.k_norm_w, e1);
+        }
         if (a.q_bias.data) {
           const m3_tensor& qb_ = a.q_bias;
           const m3_tensor& kb_ = a.k_bias;
@@ -543,7 +614,7 @@ static cudaError_t launch_step_r(const m3_step_args& a, cudaStream_t stream) {
   const long long pairs = (long long)a.batch * a.heads;
   while (rows > 4 && pairs * ((P + rows - 1) / rows) < 4 * 148) rows >>= 1;
   dim3 grid((P + rows - 1) / rows, a.heads, a.batch);
-  const size_t smem = (128 + 3 * (size_t)R * N) * sizeof(float);
+  const size_t smem = (128 + 3 * (size_t)R * N + 2 * R) * sizeof(float);
   auto go = [&](auto kern) -> cudaError_t {
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

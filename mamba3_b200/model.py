@@ -283,23 +283,31 @@ class _Mamba3Mixer(nn.Module):
     def step(self, hidden_states: torch.Tensor, cache: _LayerCache | None):
         if hidden_states.ndim != 3 or hidden_states.shape[1:] != (1, self.d_model):
             raise ValueError(f"expected [batch, 1, {self.d_model}], got {tuple(hidden_states.shape)}")
+        if cache is not None:
+            self._validate_cache(cache, hidden_states.shape[0])
+        if self._use_kernels(hidden_states):
+            # Model mode: B/C RMS-norm, softplus(delta + dt_bias), the heavy-tail decay, bias and
+            # rotation all happen in the kernel, on raw views of the projection (q/k unexpanded,
+            # stride 0 over heads).
+            z, x, B, C, delta, decay, trap, angles = self._views(self.in_proj(hidden_states))
+            if cache is None:
+                cache = self.allocate_cache(hidden_states.shape[0], device=hidden_states.device, dtype=x.dtype)
+            if cache[2].dtype == C.dtype and cache[3].dtype == x.dtype:
+                heads = self.nheads
+                qh = C[:, 0].expand(-1, heads, -1, -1) if C.shape[2] == 1 else C[:, 0].repeat_interleave(
+                    heads // C.shape[2], dim=1)
+                kh = B[:, 0].expand(-1, heads, -1, -1) if B.shape[2] == 1 else B[:, 0].repeat_interleave(
+                    heads // B.shape[2], dim=1)
+                mixed, next_cache = _step_device(
+                    qh, kh, x[:, 0], z[:, 0], decay[:, 0], delta[:, 0], trap[:, 0], angles[:, 0], self.D, cache,
+                    mimo_x=self.mimo_x, mimo_z=self.mimo_z, mimo_out=self.mimo_out, q_bias=self.C_bias,
+                    k_bias=self.B_bias, out_state=cache[1] if self._state_in_place else None,
+                    q_norm_w=self.C_norm.weight, k_norm_w=self.B_norm.weight, dt_bias=self.dt_bias,
+                    norm_eps=self.C_norm.eps)
+                return self.out_proj(mixed.flatten(-2)).unsqueeze(1), next_cache
         q, k, x, z, adt, dt, trap, angles = self._project(hidden_states)
         if cache is None:
             cache = self.allocate_cache(hidden_states.shape[0], device=hidden_states.device, dtype=x.dtype)
-        else:
-            self._validate_cache(cache, hidden_states.shape[0])
-        if self._use_kernels(hidden_states) and cache[2].dtype == q.dtype and cache[3].dtype == x.dtype:
-            # Bias and rotation happen in the kernel; q/k stay unexpanded views (stride 0 over heads).
-            heads = self.nheads
-            qh = q[:, 0].expand(-1, heads, -1, -1) if q.shape[2] == 1 else q[:, 0].repeat_interleave(
-                heads // q.shape[2], dim=1)
-            kh = k[:, 0].expand(-1, heads, -1, -1) if k.shape[2] == 1 else k[:, 0].repeat_interleave(
-                heads // k.shape[2], dim=1)
-            mixed, next_cache = _step_device(
-                qh, kh, x[:, 0], z[:, 0], adt[:, 0], dt[:, 0], trap[:, 0], angles[:, 0], self.D, cache,
-                mimo_x=self.mimo_x, mimo_z=self.mimo_z, mimo_out=self.mimo_out, q_bias=self.C_bias,
-                k_bias=self.B_bias, out_state=cache[1] if self._state_in_place else None)
-            return self.out_proj(mixed.flatten(-2)).unsqueeze(1), next_cache
         q, k = self._expand_qk(q, k)
         fused = fused_step(q[:, 0], k[:, 0], x[:, 0], z[:, 0], adt[:, 0], dt[:, 0], trap[:, 0], angles[:, 0], self.D,
                            cache, mimo_x=self.mimo_x, mimo_z=self.mimo_z, mimo_out=self.mimo_out)

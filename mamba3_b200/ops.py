@@ -337,7 +337,11 @@ def _validate_fused_step(q, k, value, gate, adt, dt, trap_logits, angle_rate, D,
 
 
 def _step_device(q, k, value, gate, adt, dt, trap_logits, angle_rate, D, cache, *, mimo_x, mimo_z, mimo_out,
-                 q_bias=None, k_bias=None, out_state=None):
+                 q_bias=None, k_bias=None, out_state=None, q_norm_w=None, k_norm_w=None, dt_bias=None,
+                 norm_eps=1e-5):
+    """Launch ``m3_step_fwd``. With ``dt_bias`` given, ``adt``/``dt`` are the raw decay/delta
+    logits and the kernel discretises them; with ``q_norm_w``/``k_norm_w`` given, ``q``/``k``
+    are the raw C/B rows and the kernel RMS-normalises them (model mode)."""
     phase, state, prev_k, prev_value = cache
     batch, heads, rank, d_state = q.shape
     y = torch.empty(value.shape, device=value.device, dtype=value.dtype)
@@ -345,13 +349,16 @@ def _step_device(q, k, value, gate, adt, dt, trap_logits, angle_rate, D, cache, 
     out_k = torch.empty(batch, heads, rank, d_state, device=q.device, dtype=q.dtype)
     if out_state is None:
         out_state = torch.empty(state.shape, device=state.device, dtype=torch.float32)
-    tensors = dict(q=q, k=k, q_bias=q_bias, k_bias=k_bias, value=value, gate=gate, adt=adt.float(),
-                   dt=dt.float(), trap=trap_logits, angle_rate=angle_rate, D=D, mimo_x=mimo_x, mimo_z=mimo_z,
+    if dt_bias is None:
+        adt, dt = adt.float(), dt.float()
+    tensors = dict(q=q, k=k, q_bias=q_bias, k_bias=k_bias, value=value, gate=gate, adt=adt,
+                   dt=dt, trap=trap_logits, angle_rate=angle_rate, D=D, mimo_x=mimo_x, mimo_z=mimo_z,
                    mimo_out=mimo_out, phase=phase, state=state, prev_k=prev_k, prev_value=prev_value, y=y,
-                   out_phase=out_phase, out_state=out_state, out_k=out_k)
+                   out_phase=out_phase, out_state=out_state, out_k=out_k, q_norm_w=q_norm_w,
+                   k_norm_w=k_norm_w, dt_bias=dt_bias)
     sizes = dict(batch=batch, heads=heads, rank=rank, d_state=d_state, head_dim=value.shape[-1],
                  num_angles=angle_rate.shape[-1])
-    _ext.step_forward(sizes=sizes, tensors=tensors)
+    _ext.step_forward(sizes=sizes, tensors=tensors, norm_eps=norm_eps)
     global LAST_STEP_DISPATCH
     LAST_STEP_DISPATCH = True
     return y, (out_phase, out_state, out_k, value)

@@ -37,7 +37,7 @@ def test_struct_layout_matches_header():
     # 12 ints + float + int, then 26 tensor descriptors of 64 bytes.
     assert ctypes.sizeof(_ext.M3Tensor) == 64
     assert ctypes.sizeof(_ext.ScanArgs) == 14 * 4 + 27 * 64
-    assert ctypes.sizeof(_ext.StepArgs) == 8 * 4 + 23 * 64
+    assert ctypes.sizeof(_ext.StepArgs) == 8 * 4 + 26 * 64
 
 
 def test_null_and_invalid_arguments_are_rejected_without_a_device():

@@ -11,6 +11,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 import torch
+import torch.nn.functional as F
 
 from conftest import load_golden, rel_err
 from mamba3_b200 import _ext, ops
@@ -197,3 +198,43 @@ def test_step_large_batches_against_oracle(batch, heads):
     ye, (phe, se, ke, _) = O.fused_step(npy(q), npy(k), npy(v), npy(z), npy(adt), npy(dt), npy(tr), npy(ang),
                                         npy(D), tuple(map(npy, cache)))
     assert rel_err(y, ye) < 1e-4 and rel_err(st, se) < 1e-4 and rel_err(kr, ke) < 1e-4
+
+
+@pytest.mark.parametrize("rank", [1, 4])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("two_pass", [True, False])
+def test_step_model_mode_matches_preprocessed_inputs(rank, dtype, two_pass):
+    """Raw projection rows + norm weights + dt_bias in the kernel == the same math done first in torch."""
+    g = torch.Generator().manual_seed(7 + rank)
+    batch, heads, n, p, s = 5, 6, 128, 64, 32 if rank == 1 else 32
+    t = lambda *shape: torch.randn(*shape, generator=g).cuda()
+    C, B = t(batch, 1, rank, n).to(dtype) * 3, t(batch, 1, rank, n).to(dtype)
+    wq, wk = 1 + 0.1 * t(n), 1 + 0.1 * t(n)
+    qb, kb = 1 + 0.1 * t(heads, rank, n), 1 + 0.1 * t(heads, rank, n)
+    v, z = t(batch, heads, p).to(dtype), t(batch, heads, p).to(dtype)
+    delta, decay, bias = t(batch, heads).to(dtype), t(batch, heads).to(dtype), 0.5 * t(heads)
+    tr, ang, D = t(batch, heads).to(dtype), t(batch, s).to(dtype), t(heads)
+    mimo = {}
+    if rank > 1:
+        mimo = dict(mimo_x=t(heads, rank, p) / rank, mimo_z=t(heads, rank, p), mimo_out=t(heads, rank, p) / rank)
+    else:
+        mimo = dict(mimo_x=None, mimo_z=None, mimo_out=None)
+    state = 0.1 * t(batch, heads, p, n)
+    if not two_pass:  # a state with a non-unit inner stride runs the single-pass kernel
+        state = state.transpose(2, 3).contiguous().transpose(2, 3)
+    cache = (t(batch, heads, s) * 2, state, t(batch, heads, rank, n).to(dtype), t(batch, heads, p).to(dtype))
+    eps = 1e-5
+    with torch.inference_mode():
+        qn = F.rms_norm(C, (n,), wq.to(dtype), eps).to(dtype)
+        kn = F.rms_norm(B, (n,), wk.to(dtype), eps).to(dtype)
+        dt = F.softplus(delta.float() + bias)
+        adt = (-ops.heavy_tail_activation(decay.float())).clamp(max=-1e-4) * dt
+        ex = lambda x: x.expand(-1, heads, -1, -1)
+        y0, c0 = ops._step_device(ex(qn), ex(kn), v, z, adt, dt, tr, ang, D, cache, q_bias=qb, k_bias=kb, **mimo)
+        y1, c1 = ops._step_device(ex(C), ex(B), v, z, decay, delta, tr, ang, D, cache, q_bias=qb, k_bias=kb,
+                                  q_norm_w=wq, k_norm_w=wk, dt_bias=bias, norm_eps=eps, **mimo)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert rel_err(y1.float(), y0.float()) < tol
+    assert rel_err(c1[1], c0[1]) < tol
+    assert rel_err(c1[2].float(), c0[2].float()) < tol
+    torch.testing.assert_close(c1[0], c0[0], rtol=1e-5, atol=1e-5)
