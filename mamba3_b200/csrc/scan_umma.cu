@@ -29,13 +29,6 @@
 //
 // Synchronisation: one mbarrier tracks tcgen05.commit of each MMA group; every wait on it is
 // bounded by %globaltimer (2 s) and sets the library's device error word instead of hanging.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include <cstring>
-#include <initializer_list>
-#include <mutex>
-
 #include "scan_common.cuh"
 
 namespace m3 {
@@ -56,36 +49,20 @@ int read_device_error(int clear) {
 
 namespace umma {
 
-// Optional per-section cycle counters of CTA (0, 0): the epilogue group's thread 0 (slots 0-15)
-// and the stage group's thread 256 (slots 16-31). Probe builds only.
+// Optional per-section cycle counters of CTA (0, 0), thread 0 (probe builds only).
 #ifdef M3_SECTION_TIMING
-__device__ unsigned long long g_section_cycles[64];
-#define M3_MARK_INIT                \
-  long long mark_prev_ = clock64(); \
-  unsigned int mark_acc_[16];       \
-  for (int k_ = 0; k_ < 16; ++k_) mark_acc_[k_] = 0
-#define M3_MARK(k)                                            \
-  do {                                                        \
-    const long long now_ = clock64();                         \
-    mark_acc_[(k) & 15] += (unsigned int)(now_ - mark_prev_); \
-    mark_prev_ = now_;                                        \
-  } while (0)
-// thread 256 i of CTA (0, 0) adds its counters to slots [16 i, 16 i + 16)
-#define M3_MARK_FLUSH                                                                                       \
-  do {                                                                                                      \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && (threadIdx.x & 255) == 0)                                     \
-      for (int k_ = 0; k_ < 16; ++k_)                                                                       \
-        atomicAdd(&g_section_cycles[16 * (threadIdx.x >> 8) + k_], (unsigned long long)mark_acc_[k_]);       \
+__device__ unsigned long long g_section_cycles[16];
+#define M3_MARK(k)                                                                    \
+  do {                                                                                \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {                     \
+      const long long now_ = clock64();                                               \
+      g_section_cycles[k] += (unsigned long long)(now_ - mark_prev_);                 \
+      mark_prev_ = now_;                                                              \
+    }                                                                                 \
   } while (0)
 #else
 #define M3_MARK(k) \
   do {             \
-  } while (0)
-#define M3_MARK_INIT \
-  do {               \
-  } while (0)
-#define M3_MARK_FLUSH \
-  do {                \
   } while (0)
 #endif
 
@@ -190,13 +167,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   for (uint32_t i = 0;; ++i) {
     uint32_t done;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(done)
-        : "r"(bar), "r"(parity), "r"(20000u)  // suspend up to 20 us per try: no issue slots while waiting
+        : "r"(bar), "r"(parity)
         : "memory");
     if (done) return true;
-    if ((i & 15u) == 15u && global_ns() - start > 2000000000ull) {
+    if ((i & 255u) == 255u && global_ns() - start > 2000000000ull) {
       atomicExch(&g_device_error, kErrMbarTimeout);
       return false;
     }
@@ -367,228 +344,102 @@ __global__ void __launch_bounds__(256) token_prep_kernel(const m3_scan_args a, f
 // x - 2pi * trunc(x / 2pi): the remainder of fmod (exact for |x| < 2pi, a few ulp beyond).
 __device__ __forceinline__ float fmod_2pi(float x) { return x - kTwoPi * truncf(x * (1.0f / kTwoPi)); }
 
-// ---------------------------------------------------------------------------------------------
-// Warp-specialised pipeline. One CTA (24 warps) per (batch, head), one CTA per SM.
-//   prep group (warps 16-23): per tile u — the TMA loads of tile u + 1, per-token scalars and the
-//     decay factorisation, the phases as packed (cos, sin) words.
-//   stage group (warps 8-15): per tile u — Q'/K'/V staging in place in slot u % 3.
-//   epilogue group (warps 0-7): per tile t — W from the scores, MMA 2 (intra), the state snapshot
-//     and MMA group 1 (scores, inter, state update) of tile t + 1, the output epilogue of tile t.
-// The groups hand tiles over through mbarriers, so the prep of tile u + 1, the staging of tile u
-// and the W / epilogue of tile u - 1 overlap. Raw rows land in three rotating slots.
-// TMEM: scores / intra of tile t in columns [64 (t % 2), +64), inter in [128 + 64 (t % 2), +64),
-// the state (S / phi, transposed) in [256, 320).
-// ---------------------------------------------------------------------------------------------
-constexpr int kPipeThreads = 800;  // epilogue and stage groups of 8 warps, prep group of 9
-constexpr int kPrepThreads = 288;
-constexpr int kPNumBars = 13;     // mbarriers of the pipeline
-constexpr uint32_t kPColS = 0, kPColI = 128, kPColX = 256, kPTmemCols = 512;
-// Per-tile scalars shared by the groups (floats): slot [3] of
-constexpr int kPCumL2 = 0, kPDiag = 64, kPEcum = 128, kPFq = 192, kPFk = 256, kPEdec = 320, kPMode = 384,
-              kPScal = 392;
-// Stage-group scratch (floats): dt, cum, sigma, scale, warp sums, raw scalars of the tile [3][68]
-constexpr int kTSdt = 0, kTCum = 64, kTSig = 128, kTScale = 192, kTWsum = 256, kTRaw = 272, kTEnd = 272 + 3 * 68;
-
-template <int R> struct PLayout {
-  static constexpr int TOK = kRows / R;
-  static constexpr int WSP = ws_stride(R, kMaxAngles);
-  static constexpr uint32_t XSlot = TOK * kP * 2;                   // raw x rows of a tile (R > 1)
-  static constexpr uint32_t QK = 0;                                 // [3] Q' (16 KB) | K' (16 KB)
-  static constexpr uint32_t V = QK + 3 * 2 * kRows * kN * 2;        // [3] V 8 KB (raw x in place, R = 1)
-  static constexpr uint32_t XR = V + 3 * kRows * kP * 2;            // [3] raw x rows (R > 1)
-  static constexpr uint32_t W = XR + (R > 1 ? 3 * XSlot : 0);       // W 8 KB
-  static constexpr uint32_t V2 = W + kRows * kRows * 2;             // V2 8 KB (unfactorised tiles)
-  static constexpr uint32_t ST = V2 + kRows * kP * 2;               // St 16 KB
-  static constexpr uint32_t F = ST + kN * kP * 2;                   // float region
-  static constexpr int SC = 0;                                      // scalar slots [3][kPScal]
-  static constexpr int TMP = SC + 3 * kPScal;                       // stage scratch
-  static constexpr int CBq = TMP + kTEnd, CBk = CBq + R * kN / 2;   // packed bias words [R][64]
-  static constexpr int CMx = CBk + R * kN / 2, CMz = CMx + R * kP, CMo = CMz + R * kP;
-  static constexpr int CMxp = CMo + R * kP;                         // packed mimo_x words [R][32]
-  static constexpr int CWq = CMxp + R * kP / 2, CWk = CWq + kN / 2; // packed norm weights [64]
-  static constexpr int WSB = ((CWk + kN / 2 + 31) / 32) * 32;       // workspace row slots [3][TOK][WSP] (128 B)
-  static constexpr int SEG = WSB + 3 * TOK * WSP;                   // [8][32] sums, [8][32] offsets
-  static constexpr int CARRY = SEG + 2 * 8 * 32;                    // [32] block offset, [32] in-block sum
-  static constexpr int FEND = CARRY + 64;
-  static constexpr uint32_t BAR = F + ((FEND * 4 + 15) / 16) * 16;  // mbarriers, tmem slot, abort flag
-  static constexpr uint32_t SmemBytes = BAR + 128 + 1024;
-};
-
-// Named barriers of warp groups. bar.sync counts a warp as arrived when any of its threads arrives,
-// so every helper first reconverges the warp (a thread that waited alone on an mbarrier rejoins).
-__device__ __forceinline__ void group_bar(int id) {
-  __syncwarp();
-  asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory");
-}
-__device__ __forceinline__ void group_bar_n(int id, int count) {
-  __syncwarp();
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-// Group barrier (count threads) that also returns the OR of `pred` over the group's threads.
-__device__ __forceinline__ bool group_bar_or_n(int id, int count, bool pred) {
-  __syncwarp();
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}\n"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
-// Group barrier that also returns the OR of `pred` over the group's threads.
-__device__ __forceinline__ bool group_bar_or(int id, bool pred) {
-  __syncwarp();
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, 256, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}\n"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id)
-      : "memory");
-  return r != 0;
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void named_bar(int id, int count) {
-  __syncwarp();
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-// Tiled TMA loads (no multicast) completing on an mbarrier; coordinates innermost first.
-__device__ __forceinline__ void tma_load5(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4,
-                                          uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
-      "%6}], [%7];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void tma_load4(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                          uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-      "[%6];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
-      : "memory");
-}
-
-// Tensor maps of the row tiles: q/k [N, R, G, L, B] and x [P, H, L, B] (16-bit, 128-byte swizzle,
-// boxes of 64 columns x one tile of rows), workspace rows [WS, L, B] (float, no swizzle).
-struct alignas(64) TileMaps {
-  CUtensorMap q, k, x, ws;
-};
-
 template <typename T, int R>
-__global__ void __launch_bounds__(kPipeThreads, 1)
-    scan_pipe_kernel(const m3_scan_args a, const __grid_constant__ TileMaps tm, int vec_y) {
-  using Lay = PLayout<R>;
+__global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_args a, int vec_y) {
+  using Lay = Layout<R>;
   constexpr int TOK = Lay::TOK;
-  constexpr int kTPL = TOK > 32 ? 2 : 1;  // phase tokens per lane
+  constexpr int kRowsPerWarp = kRows / kWarps;               // staging rows per warp (8)
   constexpr bool kBf16 = DType<T>::id == M3_BF16;
   // Largest |cum - cmid| for which the decay can be split into per-row operand factors
   // e^{cum_i - cmid} (Q rows) and e^{cmid - cum_j} (K rows) without leaving the 16-bit range.
   constexpr float kLim = kBf16 ? 80.0f : 8.0f;
-  constexpr int kBarE = 1, kBarS = 2, kBarP = 3, kBarPhase = 4;  // named barriers
   const int h = blockIdx.x, b = blockIdx.y;
   const int S = a.num_angles, L = a.length;
   const int g = h / (a.heads / a.groups);
-  const bool rev = a.reverse != 0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int group = min(warp >> 3, 2);                // 0 epilogue, 1 stage, 2 prep
-  const int gw = warp & 7, gt = tid - 256 * group;    // warp / thread index inside the group
-  const int quad = warp & 3, part = (warp >> 2) & 1;  // TMEM lane quadrant, column half
-  const int WS = ws_stride(R, S);
-  constexpr int WA = ws_ang(R);
-  const int ntiles = (L + TOK - 1) / TOK;
-  // Row tiles hold tokens in memory order: smem token row i is scan position i (forward) or
-  // TOK - 1 - i (reverse scans load the tile's tokens as one ascending box).
-  auto spos = [&](int i) { return rev ? TOK - 1 - i : i; };
+  const int quad = warp & 3, part = warp >> 2;  // TMEM lane quadrant, column half
+  const int WS = ws_stride(R, S);               // workspace floats per token
+  constexpr int WA = ws_ang(R);                 // first angle slot of a workspace row
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* fsm = reinterpret_cast<float*>(smem + Lay::F);
-  float* tmp = fsm + Lay::TMP;
-  float* sdt = tmp + kTSdt;
-  float* cum = tmp + kTCum;
-  float* sig = tmp + kTSig;
-  float* wsum = tmp + kTWsum;
-  uint32_t* cbq = reinterpret_cast<uint32_t*>(fsm + Lay::CBq);
-  uint32_t* cbk = reinterpret_cast<uint32_t*>(fsm + Lay::CBk);
-  uint32_t* cwq = reinterpret_cast<uint32_t*>(fsm + Lay::CWq);
-  uint32_t* cwk = reinterpret_cast<uint32_t*>(fsm + Lay::CWk);
+  float* fsm = reinterpret_cast<float*>(smem + kOffF);
+  float* cum = fsm + kSCum;
+  float* ecum = fsm + kSEcum;
+  float* edec = fsm + kSEdec;
+  float* scale = fsm + kSScale;
+  float* diag = fsm + kSDiag;
+  float* sdt = fsm + kSDt;
+  float* wsum = fsm + kSWsum;
+  float* cum_l2 = fsm + kSCumL2;
+  float* fq = fsm + kSFq;
+  float* fk = fsm + kSFk;
+  float* mode = fsm + kSMode;  // [0] cmid, [1] cum_last, [2] factorised, [3] e^{cum_last}
+  float* sraw = fsm + kSRaw;   // raw per-token dt, adt, sigma of the next tile [3][68]
+  float* cst = fsm;
+  float* wsb = fsm + Lay::Ws;  // the tile's workspace rows; the phase replaces pi*tanh in place
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Lay::OffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::OffBar + 8);
+  int* abort_flag = reinterpret_cast<int*>(smem + Lay::OffBar + 16);
+  const uint32_t bar_addr = smem_u32(bar);
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bars = sbase + Lay::BAR;
-  // mbarriers (8 bytes each): mma1[2], mma2[2], prep[3], staged[3], tma[3]
-  const uint32_t bar_mma1 = bars, bar_mma2 = bars + 16, bar_prep = bars + 32, bar_staged = bars + 56,
-                 bar_tma = bars + 80;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::BAR + 8 * kPNumBars);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Lay::BAR + 8 * kPNumBars + 4);
   const bool has_phase = a.phase.data != nullptr || a.angles.data != nullptr;
   const bool has_ws = a.workspace.data != nullptr;
-  T* yp = static_cast<T*>(a.y.data);
-  const T* zp = static_cast<const T*>(a.gate.data);
-  const float Dh = ld_t(a.D, h * a.D.stride[0]);
-  auto scal = [&](int u) -> float* { return fsm + Lay::SC + (u % 3) * kPScal; };
-  auto wslot = [&](int u) -> float* { return fsm + Lay::WSB + (u % 3) * (TOK * Lay::WSP); };
-  auto qk_off = [&](int u) -> uint32_t { return Lay::QK + (uint32_t)(u % 3) * (2 * kRows * kN * 2); };
-  auto v_off = [&](int u) -> uint32_t { return Lay::V + (uint32_t)(u % 3) * (kRows * kP * 2); };
-  auto xr_off = [&](int u) -> uint32_t { return Lay::XR + (uint32_t)(u % 3) * Lay::XSlot; };
-  auto gwait = [&](uint32_t bar, uint32_t parity, int bid) {
-    if (gt == 0 && !mbar_wait(bar, parity)) *abort_flag = 1;
-    group_bar(bid);
-  };
-  // Barrier of a three-slot ring: tile u completes phase u / 3 of slot u % 3.
-  auto ring = [](uint32_t base, int u) { return base + 8 * (uint32_t)(u % 3); };
-  auto ring_par = [](int u) { return (uint32_t)((u / 3) & 1); };
+  const float* ws = static_cast<const float*>(a.workspace.data);
 
-  // ---- loads of tile u: one prep thread issues the TMA boxes (raw q/k rows into the Q'/K' slot, x rows
-  // into the V slot (R = 1) or the raw-x slot, workspace rows) on the slot's mbarrier ----
-  auto tma_tile = [&](int u) {
-    const int t0 = u * TOK;
-    const int ts = rev ? L - t0 - TOK : t0;  // first token of the box (may be negative: zero fill)
-    const uint32_t bar = bar_tma + 8 * (u % 3);
-    const uint32_t bytes = 4u * (kRows * 64 * 2) + Lay::XSlot + (has_ws ? (uint32_t)(TOK * WS * 4) : 0u);
-    mbar_expect_tx(bar, bytes);
-    const uint32_t qa = sbase + qk_off(u), ka = qa + kRows * kN * 2;
-    tma_load5(qa, &tm.q, 0, 0, g, ts, b, bar);
-    tma_load5(qa + kRows * 128, &tm.q, 64, 0, g, ts, b, bar);
-    tma_load5(ka, &tm.k, 0, 0, g, ts, b, bar);
-    tma_load5(ka + kRows * 128, &tm.k, 64, 0, g, ts, b, bar);
-    tma_load4(sbase + (R == 1 ? v_off(u) : xr_off(u)), &tm.x, 0, h, ts, b, bar);
-    if (has_ws) tma_load3(smem_u32(wslot(u)), &tm.ws, 0, ts, b, bar);
-  };
-  // Slot contents the TMA does not bring: workspace stand-ins and the phase tensor (prep threads).
-  auto fill_tile = [&](int u) {
-    const int t0 = u * TOK, nt = min(TOK, L - t0);
-    float* wsb = wslot(u);
-    if (!has_ws)
-      for (int i = gt; i < TOK * 2 * R; i += kPrepThreads) wsb[(i / (2 * R)) * WS + i % (2 * R)] = 1.0f;
-    if (a.phase.data) {
-      for (int i = gt; i < TOK * S; i += kPrepThreads) {
-        const int j = i / S, sidx = i % S;
-        float v = 0.0f;
-        if (j < nt) {
-          const int t = scan_token(a, t0 + j);
-          v = ld_t(a.phase, b * a.phase.stride[0] + (int64_t)t * a.phase.stride[1] + h * a.phase.stride[2] +
-                                sidx * a.phase.stride[3]);
-        }
-        wsb[spos(j) * WS + WA + sidx] = v;
+  const T* qp = static_cast<const T*>(a.q.data);
+  const T* kp = static_cast<const T*>(a.k.data);
+  const T* vp = static_cast<const T*>(a.value.data);
+  const T* zp = static_cast<const T*>(a.gate.data);
+  T* yp = static_cast<T*>(a.y.data);
+  const float Dh = ld_t(a.D, h * a.D.stride[0]);
+  // Row bases (the rows themselves are contiguous and 16-byte aligned: scan_umma_supported).
+  const int64_t q_b0 = b * a.q.stride[0] + g * a.q.stride[2];
+  const int64_t k_b0 = b * a.k.stride[0] + g * a.k.stride[2];
+  const int64_t v_b0 = b * a.value.stride[0] + h * a.value.stride[2];
+  const int64_t z_b0 = b * a.gate.stride[0] + h * a.gate.stride[2];
+  const int64_t ws_b = (int64_t)b * L * WS;
+
+  // ---- loads of a tile, issued one tile ahead (cp.async for rows; see the tile loop) ----
+  // q/k rows go straight into the Q'/K' tiles (processed in place), raw x into the W tile, z into the
+  // z tile of the tile's parity, workspace rows into wsb.
+  auto issue_qk = [&](int t0n, int ntn) {
+    constexpr int kQChunks = kRows * (kN / 8);
+    for (int c = tid; c < kQChunks; c += kThreads) {
+      const int row = c >> 4, c8 = c & 15;
+      const int j = row / R, r = row % R;
+      if (j < ntn) {
+        const int t = scan_token(a, t0n + j);
+        const uint32_t off = swz(row, c8 * 8, kRows);
+        cp_async16(sbase + kOffQ + off, qp + q_b0 + (int64_t)t * a.q.stride[1] + r * a.q.stride[3] + c8 * 8);
+        cp_async16(sbase + kOffK + off, kp + k_b0 + (int64_t)t * a.k.stride[1] + r * a.k.stride[3] + c8 * 8);
       }
     }
   };
-  // Raw scalar words (float, or the bits of a 16-bit value) and their conversion.
+  auto issue_x = [&](int t0n, int ntn) {
+    for (int c = tid; c < TOK * (kP / 8); c += kThreads) {
+      const int j = c >> 3, c8 = c & 7;
+      if (j < ntn) {
+        const int t = scan_token(a, t0n + j);
+        cp_async16(sbase + kOffW + swz(j, c8 * 8, kRows), vp + v_b0 + (int64_t)t * a.value.stride[1] + c8 * 8);
+      }
+    }
+  };
+  auto issue_z = [&](int t0n, int ntn, int par) {
+    const uint32_t zoff = kOffZ + par * (kRows * kP * 2);
+    for (int c = tid; c < TOK * (kP / 8); c += kThreads) {
+      const int j = c >> 3, c8 = c & 7;
+      if (j < ntn) {
+        const int t = scan_token(a, t0n + j);
+        cp_async16(sbase + zoff + swz(j, c8 * 8, kRows), zp + z_b0 + (int64_t)t * a.gate.stride[1] + c8 * 8);
+      }
+    }
+  };
+  // Per-token scalars of a tile: thread j <= TOK fetches the raw words of token j (j == TOK: the
+  // first token after the tile) into registers without using them, so the loads stay in flight;
+  // finish_scalars() converts them (softplus / heavy-tail / sigmoid) into sraw later.
+  uint32_t raw_dt = 0, raw_adt = 0, raw_trap = 0;
+  bool raw_ok = false;
   auto raw_word = [](const m3_tensor& t, int64_t idx) -> uint32_t {
     if (t.dtype == M3_F32) return __float_as_uint(static_cast<const float*>(t.data)[idx]);
     return (uint32_t)static_cast<const uint16_t*>(t.data)[idx];
@@ -598,23 +449,78 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
     if (dtype == M3_BF16) return __uint_as_float(w << 16);
     return __half2float(__ushort_as_half((unsigned short)w));
   };
+  auto fetch_scalars = [&](int t0n, int ntn) {
+    raw_ok = false;
+    if (tid <= TOK && t0n + tid < L && (tid < ntn || tid == TOK)) {
+      const int t = scan_token(a, t0n + tid);
+      raw_dt = raw_word(a.dt, b * a.dt.stride[0] + (int64_t)t * a.dt.stride[1] + h * a.dt.stride[2]);
+      raw_adt = raw_word(a.adt, b * a.adt.stride[0] + (int64_t)t * a.adt.stride[1] + h * a.adt.stride[2]);
+      raw_trap = raw_word(a.trap, b * a.trap.stride[0] + (int64_t)t * a.trap.stride[1] + h * a.trap.stride[2]);
+      raw_ok = true;
+    }
+  };
   const float dt_bias_h = a.dt_bias.data ? ld_t(a.dt_bias, h * a.dt_bias.stride[0]) : 0.0f;
-  // ---- set-up: TMEM (warp 0), mbarriers, per-CTA constants ----
+  auto finish_scalars = [&]() {
+    if (tid <= TOK) {
+      float dtv = 0.0f, adtv = 0.0f, sg = 0.0f;
+      if (raw_ok) {
+        if (a.dt_bias.data) {
+          // mamba3/model.py:195-198: dt = softplus(delta + dt_bias); A = -heavytail(a) clamped <= -1e-4.
+          dtv = softplusf_(word_to_f(raw_dt, a.dt.dtype) + dt_bias_h);
+          adtv = fminf(-heavy_tailf(word_to_f(raw_adt, a.adt.dtype)), -kAFloor) * dtv;
+        } else {
+          dtv = word_to_f(raw_dt, a.dt.dtype);
+          adtv = word_to_f(raw_adt, a.adt.dtype);
+        }
+        sg = sigmoidf_(word_to_f(raw_trap, a.trap.dtype));
+      }
+      sraw[tid] = dtv;
+      sraw[68 + tid] = adtv;
+      sraw[136 + tid] = sg;
+    }
+  };
+  // Workspace rows (cp.async) or their stand-ins, and the phase tensor of the op-level API.
+  auto fetch_small = [&](int t0n, int ntn) {
+    if (has_ws) {
+      const int chunks = WS / 4;  // <= 12: one 16-slot row per token, no division
+      for (int c = tid; c < TOK * 16; c += kThreads) {
+        const int j = c >> 4, c4 = c & 15;
+        if (j < ntn && c4 < chunks) {
+          const int t = scan_token(a, t0n + j);
+          cp_async16(smem_u32(wsb + j * WS + 4 * c4), ws + ws_b + (int64_t)t * WS + 4 * c4);
+        }
+      }
+    } else {
+      for (int i = tid; i < TOK * 2 * R; i += kThreads) wsb[(i / (2 * R)) * WS + i % (2 * R)] = 1.0f;
+    }
+    if (a.phase.data) {
+      for (int i = tid; i < TOK * S; i += kThreads) {
+        const int j = i / S, sidx = i % S;
+        float v = 0.0f;
+        if (j < ntn) {
+          const int t = scan_token(a, t0n + j);
+          v = ld_t(a.phase, b * a.phase.stride[0] + (int64_t)t * a.phase.stride[1] + h * a.phase.stride[2] +
+                                sidx * a.phase.stride[3]);
+        }
+        wsb[j * WS + WA + sidx] = v;
+      }
+    }
+  };
+
+  // ---- set-up: TMEM allocation (warp 0), mbarrier, per-CTA constants, phase carry ----
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kPTmemCols));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    for (int i = 0; i < kPNumBars; ++i) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bars + 8 * i));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_addr));
     asm volatile("fence.mbarrier_init.release.cluster;");
     *abort_flag = 0;
   }
-  if (tid == 512) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm.q)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm.x)) : "memory");
-  }
-  for (int i = tid; i < R * kN / 2; i += kPipeThreads) {
+  uint32_t* cbq = reinterpret_cast<uint32_t*>(cst + Lay::CBq);  // packed bias words [R][64]
+  uint32_t* cbk = reinterpret_cast<uint32_t*>(cst + Lay::CBk);
+  for (int i = tid; i < R * kN / 2; i += kThreads) {
     const int r = i / (kN / 2), n = 2 * (i % (kN / 2));
     float bq[2] = {0.0f, 0.0f}, bk[2] = {0.0f, 0.0f};
     if (a.q_bias.data) {
@@ -627,86 +533,395 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
     cbq[i] = pack2<T>(bq[0], bq[1]);
     cbk[i] = pack2<T>(bk[0], bk[1]);
   }
-  for (int i = tid; i < kN / 2; i += kPipeThreads) {
-    const bool nw = a.q_norm_w.data != nullptr;
-    cwq[i] = nw ? pack2<T>(ld_t(a.q_norm_w, 2 * i * a.q_norm_w.stride[0]), ld_t(a.q_norm_w, (2 * i + 1) * a.q_norm_w.stride[0]))
-                : 0u;
-    cwk[i] = nw ? pack2<T>(ld_t(a.k_norm_w, 2 * i * a.k_norm_w.stride[0]), ld_t(a.k_norm_w, (2 * i + 1) * a.k_norm_w.stride[0]))
-                : 0u;
-  }
   if (R > 1) {
-    for (int i = tid; i < R * kP; i += kPipeThreads) {
+    for (int i = tid; i < R * kP; i += kThreads) {
       const int r = i / kP, p = i % kP;
-      fsm[Lay::CMx + i] = ld_t(a.mimo_x, h * a.mimo_x.stride[0] + r * a.mimo_x.stride[1] + p * a.mimo_x.stride[2]);
-      fsm[Lay::CMz + i] = ld_t(a.mimo_z, h * a.mimo_z.stride[0] + r * a.mimo_z.stride[1] + p * a.mimo_z.stride[2]);
-      fsm[Lay::CMo + i] =
+      cst[Lay::CMx + i] = ld_t(a.mimo_x, h * a.mimo_x.stride[0] + r * a.mimo_x.stride[1] + p * a.mimo_x.stride[2]);
+      cst[Lay::CMz + i] = ld_t(a.mimo_z, h * a.mimo_z.stride[0] + r * a.mimo_z.stride[1] + p * a.mimo_z.stride[2]);
+      cst[Lay::CMo + i] =
           ld_t(a.mimo_out, h * a.mimo_out.stride[0] + r * a.mimo_out.stride[1] + p * a.mimo_out.stride[2]);
     }
-    uint32_t* cmxp = reinterpret_cast<uint32_t*>(fsm + Lay::CMxp);
-    for (int i = tid; i < R * kP / 2; i += kPipeThreads) {
+    uint32_t* cmxp = reinterpret_cast<uint32_t*>(cst + Lay::CMxp);
+    for (int i = tid; i < R * kP / 2; i += kThreads) {
       const int r = i / (kP / 2), p = 2 * (i % (kP / 2));
       const m3_tensor& mx = a.mimo_x;
       cmxp[i] = pack2<T>(ld_t(mx, h * mx.stride[0] + r * mx.stride[1] + p * mx.stride[2]),
                          ld_t(mx, h * mx.stride[0] + r * mx.stride[1] + (p + 1) * mx.stride[2]));
     }
   }
+  // Staging: thread (warp, lane) owns the 16-byte chunk cq = lane & 15 (elements 8 cq .. 8 cq + 7)
+  // of rows warp * 8 + 2 i + (lane >> 4). Its norm weights, packed.
+  const int cq = lane & 15;
+  const bool has_norm = a.q_norm_w.data != nullptr;
+  const bool has_bias = a.q_bias.data != nullptr;
+  uint32_t wq2[4], wk2[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int n = 8 * cq + 2 * e;
+    wq2[e] = has_norm ? pack2<T>(ld_t(a.q_norm_w, n * a.q_norm_w.stride[0]),
+                                 ld_t(a.q_norm_w, (n + 1) * a.q_norm_w.stride[0])) : 0u;
+    wk2[e] = has_norm ? pack2<T>(ld_t(a.k_norm_w, n * a.k_norm_w.stride[0]),
+                                 ld_t(a.k_norm_w, (n + 1) * a.k_norm_w.stride[0])) : 0u;
+  }
+  // Loads of the first tile.
+  {
+    const int nt0 = min(TOK, L);
+    issue_qk(0, nt0);
+    issue_x(0, nt0);
+    issue_z(0, nt0, 0);
+    fetch_small(0, nt0);
+    fetch_scalars(0, nt0);
+    finish_scalars();
+    cp_async_commit();
+  }
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+
+  // ---- initial state into TMEM: S^T[n][p] = S0[p][n] + c0 sum_r (v mx_r)[p] k_r[n] ----
+  {
+    float c0 = 0.0f;
+    if (a.initial_k.data) {
+      float dt0, adt0;
+      const int t_first = scan_token(a, 0);
+      load_dt_adt(a, b, t_first, h, dt0, adt0);
+      c0 = dt0 * (1.0f - sigmoidf_(load_trap(a, b, t_first, h)));
+    }
+    const int n = quad * 32 + lane;
+    uint32_t r32[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int p = part * 32 + j;
+      float s = 0.0f;
+      if (a.initial_state.data) {
+        const m3_tensor& t = a.initial_state;
+        s = ld_t(t, b * t.stride[0] + h * t.stride[1] + p * t.stride[2] + n * t.stride[3]);
+      }
+      if (a.initial_k.data) {
+        const m3_tensor& ik = a.initial_k;
+        const m3_tensor& iv = a.initial_value;
+        const float v = ld_t(iv, b * iv.stride[0] + h * iv.stride[1] + p * iv.stride[2]);
+        float acc = 0.0f;
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+          const float vr = R > 1 ? v * cst[Lay::CMx + rr * kP + p] : v;
+          acc += vr * ld_t(ik, b * ik.stride[0] + h * ik.stride[1] + rr * ik.stride[2] + n * ik.stride[3]);
+        }
+        s += c0 * acc;
+      }
+      r32[j] = __float_as_uint(s);
+    }
+    M3_TMEM_ST32(tmem + lane_base + kColState + part * 32, r32);
+    tmem_wait_st();
+  }
+
   const uint32_t id_scores = idesc(64, 64, kBf16, false, false);  // K-major A and B
   const uint32_t id_nmn = idesc(64, 64, kBf16, false, true);      // K-major A, MN-major B
   const uint32_t id_state = idesc(128, 64, kBf16, true, true);    // MN-major A and B
+  uint32_t phase_bit = 0;
+  float phi = 1.0f;  // TMEM holds S / phi
+#ifdef M3_SECTION_TIMING
+  long long mark_prev_ = clock64();
+#endif
 
-  if (group == 0) {
-    // =========================== epilogue group ===========================
-    // Initial state into TMEM: S^T[n][p] = S0[p][n] + c0 sum_r (v mx_r)[p] k_r[n].
-    {
-      float c0 = 0.0f;
-      if (a.initial_k.data) {
-        float dt0, adt0;
-        const int t_first = scan_token(a, 0);
-        load_dt_adt(a, b, t_first, h, dt0, adt0);
-        c0 = dt0 * (1.0f - sigmoidf_(load_trap(a, b, t_first, h)));
-      }
-      const int n = quad * 32 + lane;
-      uint32_t r32[32];
+  // Phase carry of this warp's angles 4 warp .. 4 warp + 3 (block offset, in-block sum).
+  float ph_off[4], ph_loc[4];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int p = part * 32 + j;
-        float s = 0.0f;
-        if (a.initial_state.data) {
-          const m3_tensor& t = a.initial_state;
-          s = ld_t(t, b * t.stride[0] + h * t.stride[1] + p * t.stride[2] + n * t.stride[3]);
-        }
-        if (a.initial_k.data) {
-          const m3_tensor& ik = a.initial_k;
-          const m3_tensor& iv = a.initial_value;
-          const float v = ld_t(iv, b * iv.stride[0] + h * iv.stride[1] + p * iv.stride[2]);
-          float acc = 0.0f;
+  for (int k = 0; k < 4; ++k) {
+    const int sidx = 4 * warp + k;
+    ph_off[k] = (a.initial_phase.data && sidx < S)
+                    ? ld_t(a.initial_phase, b * a.initial_phase.stride[0] + h * a.initial_phase.stride[1] +
+                                                sidx * a.initial_phase.stride[2])
+                    : 0.0f;
+    ph_loc[k] = 0.0f;
+  }
+  int tile = 0;
+  for (int t0 = 0; t0 < L; t0 += TOK, ++tile) {
+    const int nt = min(TOK, L - t0);
+    const int t0n = t0 + TOK, ntn = min(TOK, L - t0n);  // next tile (ntn <= 0: none)
+    M3_MARK(0);
+    cp_async_wait_all();  // this tile's rows, workspace rows (issued during the previous tile)
+    __syncthreads();
+    M3_MARK(1);
+
+    // ---- warp 0: per-token scalars (mamba3/ops.py:659-671) of tokens 2 lane, 2 lane + 1: cumulative
+    // decay, trapezoid scale, decay factorisation; all in registers and shuffles ----
+    if (warp == 0) {
+      const int j0 = 2 * lane;
+      float dtv[2], adv[2], sgv[2];
 #pragma unroll
-          for (int rr = 0; rr < R; ++rr) {
-            const float vr = R > 1 ? v * fsm[Lay::CMx + rr * kP + p] : v;
-            acc += vr * ld_t(ik, b * ik.stride[0] + h * ik.stride[1] + rr * ik.stride[2] + n * ik.stride[3]);
-          }
-          s += c0 * acc;
-        }
-        r32[j] = __float_as_uint(s);
+      for (int m = 0; m < 2; ++m) {
+        const bool v = j0 + m < nt;
+        dtv[m] = v ? sraw[j0 + m] : 0.0f;
+        adv[m] = v ? sraw[68 + j0 + m] : 0.0f;
+        sgv[m] = v ? sraw[136 + j0 + m] : 0.0f;
       }
-      M3_TMEM_ST32(tmem + lane_base + kPColX + part * 32, r32);
-      tmem_wait_st();
+      const float incl = warp_incl_scan(adv[0] + adv[1], lane);
+      const float cum2[2] = {incl - adv[1], incl};
+      const int jm = (nt - 1) >> 1, jl = nt - 1;
+      const float cmid = __shfl_sync(0xffffffffu, (jm & 1) ? cum2[1] : cum2[0], jm >> 1);
+      const float cl = __shfl_sync(0xffffffffu, (jl & 1) ? cum2[1] : cum2[0], jl >> 1);
+      // scale_j = gamma_j + dt_{j+1} (1 - sigma_{j+1}); the last token looks at the first one after the tile
+      const float beta_up = __shfl_down_sync(0xffffffffu, dtv[0] * (1.0f - sgv[0]), 1);
+      const float beta_next = (nt == TOK && t0 + TOK < L) ? sraw[TOK] * (1.0f - sraw[136 + TOK]) : 0.0f;
+      const float nx[2] = {j0 + 1 < nt ? dtv[1] * (1.0f - sgv[1]) : 0.0f,
+                           j0 + 2 < nt ? beta_up : ((j0 + 2 == TOK && nt == TOK) ? beta_next : 0.0f)};
+      float scv[2], dg[2], dev = 0.0f;
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const bool v = j0 + m < nt;
+        const float gamma = dtv[m] * sgv[m];
+        scv[m] = v ? gamma + nx[m] : 0.0f;
+        dg[m] = v ? gamma / scv[m] : 0.0f;
+        if (v) dev = fmaxf(dev, fabsf(cum2[m] - cmid));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dev = fmaxf(dev, __shfl_xor_sync(0xffffffffu, dev, o));
+      const bool fct = dev <= kLim;
+      if (j0 < TOK) {
+        float o_fq[2], o_fk[2], o_ec[2], o_ed[2];
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          const bool v = j0 + m < nt;
+          const float c = cum2[m];
+          o_fq[m] = v ? (fct ? __expf(c - cmid) : 1.0f) : 0.0f;
+          o_fk[m] = v ? (fct ? scv[m] * __expf(cmid - c) : scv[m]) : 0.0f;
+          o_ec[m] = v ? (fct ? __expf(cmid) : __expf(c)) : 0.0f;
+          o_ed[m] = (v && !fct) ? __expf(cl - c) : 0.0f;
+        }
+        *reinterpret_cast<float2*>(sdt + j0) = make_float2(dtv[0], dtv[1]);
+        *reinterpret_cast<float2*>(cum_l2 + j0) = make_float2(cum2[0] * kLog2e, cum2[1] * kLog2e);
+        *reinterpret_cast<float2*>(diag + j0) = make_float2(dg[0], dg[1]);
+        *reinterpret_cast<float2*>(fq + j0) = make_float2(o_fq[0], o_fq[1]);
+        *reinterpret_cast<float2*>(fk + j0) = make_float2(o_fk[0], o_fk[1]);
+        *reinterpret_cast<float2*>(ecum + j0) = make_float2(o_ec[0], o_ec[1]);
+        *reinterpret_cast<float2*>(edec + j0) = make_float2(o_ed[0], o_ed[1]);
+      }
+      if (lane == 0) {
+        mode[0] = cmid;
+        mode[1] = cl;
+        mode[2] = fct ? 1.0f : 0.0f;
+        mode[3] = __expf(cl);
+      }
     }
-    float phi = 1.0f;  // TMEM holds S / phi
-    // Snapshot before tile u: St = bf16(S) (the state MMA 1 of tile u reads), X *= state_mult.
-    auto snapshot = [&](int u) {
-      const float* sc = scal(u);
-      const bool fact = sc[kPMode + 2] != 0.0f;
-      const float cmid = sc[kPMode], cl = sc[kPMode + 1];
-      const float state_mult = (fact ? expf(cmid) : sc[kPMode + 3]) * phi;
+    __syncthreads();
+    M3_MARK(2);
+    // ---- phases -> packed (cos, sin) words over pi*tanh(angle) in wsb. Warp w: angles 4 w .. 4 w + 3
+    // (carried block offset and in-block sum in registers, mamba3/model.py:246-251); lane: tokens
+    // 2 lane, 2 lane + 1. SISO: word m = (cos_m, sin_m); MIMO (S == 32): word q < 16 = (cos_2q, cos_2q+1),
+    // word 16 + q = (sin_2q, sin_2q+1), the element pairs a staging word holds. ----
+    if (has_phase) {
+      const int s0 = 4 * warp, j0 = 2 * lane;
+      float ph[2][4];
+      if (s0 < S) {
+        if (a.angles.data) {
+          if (t0 > 0 && (t0 % kPhaseBlock) == 0) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              ph_off[k] = fmodf(ph_off[k] + ph_loc[k], kTwoPi);
+              ph_loc[k] = 0.0f;
+            }
+          }
+          float inc[2][4];
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const int j = j0 + m;
+            float4 av = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float dtj = 0.0f;
+            if (j < nt) {
+              av = *reinterpret_cast<const float4*>(wsb + j * WS + WA + s0);
+              dtj = sdt[j];
+            }
+            const float in[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) inc[m][k] = s0 + k < S ? fmod_2pi(in[k] * dtj) : 0.0f;
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float x = warp_incl_scan(inc[0][k] + inc[1][k], lane);
+            const float tot = __shfl_sync(0xffffffffu, x, 31);
+            ph[0][k] = fmod_2pi((ph_loc[k] + (x - inc[1][k])) + ph_off[k]);
+            ph[1][k] = fmod_2pi((ph_loc[k] + x) + ph_off[k]);
+            ph_loc[k] += tot;
+          }
+        } else {
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const int j = j0 + m;
+            float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (j < TOK) pv = *reinterpret_cast<const float4*>(wsb + j * WS + WA + s0);
+            ph[m][0] = pv.x;
+            ph[m][1] = pv.y;
+            ph[m][2] = pv.z;
+            ph[m][3] = pv.w;
+          }
+        }
+      }
+      if (a.mimo_rotation) __syncthreads();  // MIMO words land on other warps' angle slots
+      if (s0 < S) {
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          const int j = j0 + m;
+          if (j < TOK) {
+            float cs[4], sn[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) __sincosf(ph[m][k], &sn[k], &cs[k]);  // |phase| < 2 pi
+            if (t0 + j == L - 1 && a.final_phase.data) {
+              const m3_tensor& fp = a.final_phase;
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                if (s0 + k < S)
+                  static_cast<float*>(fp.data)[b * fp.stride[0] + h * fp.stride[1] + (s0 + k) * fp.stride[2]] =
+                      ph[m][k];
+            }
+            uint32_t* w = reinterpret_cast<uint32_t*>(wsb + j * WS + WA);
+            if (a.mimo_rotation) {
+              *reinterpret_cast<uint2*>(w + s0 / 2) = make_uint2(pack2<T>(cs[0], cs[1]), pack2<T>(cs[2], cs[3]));
+              *reinterpret_cast<uint2*>(w + 16 + s0 / 2) = make_uint2(pack2<T>(sn[0], sn[1]), pack2<T>(sn[2], sn[3]));
+            } else if (s0 + 4 <= S) {
+              *reinterpret_cast<uint4*>(w + s0) = make_uint4(pack2<T>(cs[0], sn[0]), pack2<T>(cs[1], sn[1]),
+                                                             pack2<T>(cs[2], sn[2]), pack2<T>(cs[3], sn[3]));
+            } else {
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                if (s0 + k < S) w[s0 + k] = pack2<T>(cs[k], sn[k]);
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();
+    const bool fact = mode[2] != 0.0f;
+    M3_MARK(3);
+
+    // ---- stage Q', K' in place (packed 16-bit math): q' = rot(q rq w + b) fq, k' = rot(k rk w + b) fk ----
+#pragma unroll
+    for (int it = 0; it < kRowsPerWarp / 2; ++it) {
+      const int row = warp * kRowsPerWarp + 2 * it + (lane >> 4);
+      const int j = row / R, r = row % R;
+      const bool valid = j < nt;
+      const int jc = min(j, TOK - 1);
+      const float* wrow = wsb + jc * WS;
+      const uint32_t off = swz(row, 8 * cq, kRows);
+      const uint4 qraw = *reinterpret_cast<const uint4*>(smem + kOffQ + off);
+      const uint4 kraw = *reinterpret_cast<const uint4*>(smem + kOffK + off);
+      uint32_t qv[4] = {qraw.x, qraw.y, qraw.z, qraw.w};
+      uint32_t kv[4] = {kraw.x, kraw.y, kraw.z, kraw.w};
+      if (has_norm) {
+        const uint32_t rq2 = bcast2<T>(wrow[r]), rk2 = bcast2<T>(wrow[R + r]);
+        const uint4 bq = *reinterpret_cast<const uint4*>(cbq + r * (kN / 2) + 4 * cq);
+        const uint4 bk = *reinterpret_cast<const uint4*>(cbk + r * (kN / 2) + 4 * cq);
+        const uint32_t bqa[4] = {bq.x, bq.y, bq.z, bq.w}, bka[4] = {bk.x, bk.y, bk.z, bk.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          qv[e] = fma2<T>(mul2<T>(qv[e], rq2), wq2[e], bqa[e]);
+          kv[e] = fma2<T>(mul2<T>(kv[e], rk2), wk2[e], bka[e]);
+        }
+      } else if (has_bias) {
+        const uint4 bq = *reinterpret_cast<const uint4*>(cbq + r * (kN / 2) + 4 * cq);
+        const uint4 bk = *reinterpret_cast<const uint4*>(cbk + r * (kN / 2) + 4 * cq);
+        const uint32_t bqa[4] = {bq.x, bq.y, bq.z, bq.w}, bka[4] = {bk.x, bk.y, bk.z, bk.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          qv[e] = add2<T>(qv[e], bqa[e]);
+          kv[e] = add2<T>(kv[e], bka[e]);
+        }
+      }
+      if (has_phase) {
+        const uint32_t* rw = reinterpret_cast<const uint32_t*>(wrow + WA);
+        if (a.mimo_rotation) {
+          // pairs (n, n + 64) for n < 32: the partner chunk is cq ^ 8, i.e. lane ^ 8.
+          uint32_t qo[4], ko[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            qo[e] = __shfl_xor_sync(0xffffffffu, qv[e], 8);
+            ko[e] = __shfl_xor_sync(0xffffffffu, kv[e], 8);
+          }
+          if ((cq & 7) < 4) {
+            const int q4 = 4 * (cq & 3);  // first cos/sin word of this chunk's angles
+            const uint4 c4 = *reinterpret_cast<const uint4*>(rw + q4);
+            const uint4 s4 = *reinterpret_cast<const uint4*>(rw + 16 + q4);
+            const uint32_t ca[4] = {c4.x, c4.y, c4.z, c4.w}, sa[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (cq < 8) {  // first half: a c - b s
+                const uint32_t ns = sa[e] ^ 0x80008000u;
+                qv[e] = fma2<T>(qo[e], ns, mul2<T>(qv[e], ca[e]));
+                kv[e] = fma2<T>(ko[e], ns, mul2<T>(kv[e], ca[e]));
+              } else {       // second half: a s + b c
+                qv[e] = fma2<T>(qo[e], sa[e], mul2<T>(qv[e], ca[e]));
+                kv[e] = fma2<T>(ko[e], sa[e], mul2<T>(kv[e], ca[e]));
+              }
+            }
+          }
+        } else if (4 * cq < S) {
+          // adjacent pairs (2m, 2m + 1), m = 4 cq + e
+          const uint4 c4 = *reinterpret_cast<const uint4*>(rw + 4 * cq);
+          const uint32_t csa[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (4 * cq + e < S) {
+              const uint32_t cc = __byte_perm(csa[e], 0, 0x1010);
+              const uint32_t ms = __byte_perm(csa[e], 0, 0x3232) ^ 0x00008000u;
+              qv[e] = rot_pair<T>(qv[e], cc, ms);
+              kv[e] = rot_pair<T>(kv[e], cc, ms);
+            }
+          }
+        }
+      }
+      if (valid && a.final_k.data && t0 + j == L - 1) {
+        const m3_tensor& fkt = a.final_k;
+        T* fkp = static_cast<T*>(fkt.data) + b * fkt.stride[0] + h * fkt.stride[1] + r * fkt.stride[2];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = 8 * cq + 2 * e;
+          fkp[n * fkt.stride[3]] = from_f<T>(lo16<T>(kv[e]));
+          fkp[(n + 1) * fkt.stride[3]] = from_f<T>(hi16<T>(kv[e]));
+        }
+      }
+      // Rows past the end are zeroed by selection: their shared memory holds stale bytes.
+      const uint32_t fq2 = bcast2<T>(fq[jc]), fk2 = bcast2<T>(fk[jc]);
+      uint4 qo4 = make_uint4(0, 0, 0, 0), ko4 = make_uint4(0, 0, 0, 0);
+      if (valid) {
+        qo4 = make_uint4(mul2<T>(qv[0], fq2), mul2<T>(qv[1], fq2), mul2<T>(qv[2], fq2), mul2<T>(qv[3], fq2));
+        ko4 = make_uint4(mul2<T>(kv[0], fk2), mul2<T>(kv[1], fk2), mul2<T>(kv[2], fk2), mul2<T>(kv[3], fk2));
+      }
+      *reinterpret_cast<uint4*>(smem + kOffQ + off) = qo4;
+      *reinterpret_cast<uint4*>(smem + kOffK + off) = ko4;
+    }
+    // ---- V = x mx_r from the raw x rows parked in the W tile; V2 = V e^{cum_last - cum} when the tile
+    // is not factorised. 16-byte chunks: 64 rows x 8 chunks over 256 threads. ----
+#pragma unroll
+    for (int c = tid; c < kRows * (kP / 8); c += kThreads) {
+      const int row = c >> 3, ch = c & 7;
+      const int j = row / R, r = row % R;
+      const int jc = min(j, TOK - 1);
+      uint4 v4 = make_uint4(0, 0, 0, 0);
+      if (j < nt) v4 = *reinterpret_cast<const uint4*>(smem + kOffW + swz(j, 8 * ch, kRows));
+      if (R > 1) {
+        const uint4 m4 = *reinterpret_cast<const uint4*>(
+            reinterpret_cast<const uint32_t*>(cst + Lay::CMxp) + r * (kP / 2) + 4 * ch);
+        v4 = make_uint4(mul2<T>(v4.x, m4.x), mul2<T>(v4.y, m4.y), mul2<T>(v4.z, m4.z), mul2<T>(v4.w, m4.w));
+      }
+      *reinterpret_cast<uint4*>(smem + kOffV + swz(row, 8 * ch, kRows)) = v4;
+      if (!fact) {
+        const uint32_t e2 = bcast2<T>(edec[jc]);
+        *reinterpret_cast<uint4*>(smem + kOffV2 + swz(row, 8 * ch, kRows)) =
+            make_uint4(mul2<T>(v4.x, e2), mul2<T>(v4.y, e2), mul2<T>(v4.z, e2), mul2<T>(v4.w, e2));
+      }
+    }
+    M3_MARK(4);
+
+    // ---- state: TMEM X (S = phi X) -> St = S in 16 bits (state before this tile); X *= factor ----
+    const float cmid = mode[0], cl = mode[1];
+    const float state_mult = (fact ? expf(cmid) : mode[3]) * phi;
+    const float phi_new = fact ? expf(cl - cmid) : 1.0f;
+    {
       uint32_t r32[32];
       fence_after();
-      M3_TMEM_LD32(tmem + lane_base + kPColX + part * 32, r32);
+      M3_TMEM_LD32(tmem + lane_base + kColState + part * 32, r32);
       tmem_wait_ld();
       const int n = quad * 32 + lane;
 #pragma unroll
@@ -715,660 +930,215 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           w[i] = pack2<T>(__uint_as_float(r32[c * 8 + 2 * i]) * phi, __uint_as_float(r32[c * 8 + 2 * i + 1]) * phi);
-        *reinterpret_cast<uint4*>(smem + Lay::ST + swz(n, part * 32 + c * 8, kN)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(smem + kOffST + swz(n, part * 32 + c * 8, kN)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j) r32[j] = __float_as_uint(__uint_as_float(r32[j]) * state_mult);
-      M3_TMEM_ST32(tmem + lane_base + kPColX + part * 32, r32);
+      M3_TMEM_ST32(tmem + lane_base + kColState + part * 32, r32);
       tmem_wait_st();
-      phi = fact ? expf(cl - cmid) : 1.0f;
-      fence_async_smem();
-    };
-    // MMA group 1 of tile u (one thread): scores = Q' K'^T, inter = Q' St, X += K'^T V (or V2).
-    auto mma_group1 = [&](int u) {
-      const bool fact = scal(u)[kPMode + 2] != 0.0f;
-      const uint32_t colS = kPColS + 64 * (u & 1), colI = kPColI + 64 * (u & 1);
-      const uint32_t qa = sbase + qk_off(u), ka = qa + kRows * kN * 2;
-      const uint32_t vsrc = fact ? sbase + v_off(u) : sbase + Lay::V2;
-      uint64_t dq[8], dk[8], ds[8], dkm[4], dv[4];
+    }
+    phi = phi_new;
+    fence_async_smem();
+    fence_before();
+    __syncthreads();
+    M3_MARK(5);
+
+    // ---- MMA group 1: scores = Q' K'^T, inter = Q' St, X += K'^T V (or V2) ----
+    if (tid == 0) {
+      fence_after();
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
+      for (int kk = 0; kk < kN / 16; ++kk) {
         const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-        dq[kk] = sdesc(qa + koff, 16, 1024);
-        dk[kk] = sdesc(ka + koff, 16, 1024);
-        ds[kk] = sdesc(sbase + Lay::ST + kk * 2048, kN * 128, 1024);
+        mma_f16(tmem + kColScores, sdesc(sbase + kOffQ + koff, 16, 1024), sdesc(sbase + kOffK + koff, 16, 1024),
+                id_scores, kk > 0);
       }
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        dkm[kk] = sdesc(ka + kk * 2048, kRows * 128, 1024);
-        dv[kk] = sdesc(vsrc + kk * 2048, kRows * 128, 1024);
+      for (int kk = 0; kk < kN / 16; ++kk) {
+        const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+        mma_f16(tmem + kColInter, sdesc(sbase + kOffQ + koff, 16, 1024),
+                sdesc(sbase + kOffST + kk * 2048, kN * 128, 1024), id_nmn, kk > 0);
       }
+      const uint32_t vsrc = fact ? kOffV : kOffV2;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) mma_f16(tmem + colS, dq[kk], dk[kk], id_scores, kk > 0);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) mma_f16(tmem + colI, dq[kk], ds[kk], id_nmn, kk > 0);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) mma_f16(tmem + kPColX, dkm[kk], dv[kk], id_state, 1);
-      mma_commit(bar_mma1 + 8 * (u & 1));
-    };
-    // Snapshot of tile u, then (once the stage group has staged it) its MMA group 1.
-    auto launch_tile = [&](int u, auto&& mark) {
-      gwait(ring(bar_prep, u), ring_par(u), kBarE);
-      mark(3);
-      snapshot(u);
-      fence_before();
-      group_bar(kBarE);
-      mark(9);
-      if (gt == 0) {
-        if (mbar_wait(ring(bar_staged, u), ring_par(u))) {
-          mark(10);
-          fence_after();
-          mma_group1(u);
-        } else {
-          *abort_flag = 1;
-        }
+      for (int kk = 0; kk < kRows / 16; ++kk) {
+        mma_f16(tmem + kColState, sdesc(sbase + kOffK + kk * 2048, kRows * 128, 1024),
+                sdesc(sbase + vsrc + kk * 2048, kRows * 128, 1024), id_state, 1);
       }
-    };
-    M3_MARK_INIT;
-#ifdef M3_SECTION_TIMING
-    auto mark = [&](int k) { M3_MARK(k); };
-#else
-    auto mark = [](int) {};
-#endif
-    launch_tile(0, mark);
-    for (int t = 0; t < ntiles; ++t) {
-      const int t0 = t * TOK, nt = min(TOK, L - t0);
-      const float* sc = scal(t);
-      const uint32_t colS = kPColS + 64 * (t & 1), colI = kPColI + 64 * (t & 1);
-      M3_MARK(7);
-      gwait(bar_mma1 + 8 * (t & 1), (t >> 1) & 1, kBarE);
-      fence_after();
-      M3_MARK(0);
-      const bool fact = sc[kPMode + 2] != 0.0f;
-      // ---- W = scores o decay -> smem (16-bit, K-major). Thread: row quad * 16 + (lane & 15),
-      // columns c0 .. c0 + 15 with c0 = part * 32 + (lane >> 4) * 16. Entry (i, k) is causal when
-      // the scan position of column k's token is at most that of row i's token. ----
-      {
-        const int i = quad * 16 + (lane & 15);
-        const int ti = spos(i / R);
-        const int c0 = part * 32 + (lane >> 4) * 16;
-        // warp-uniform: every column token is later in scan order than every row token
-        const bool all_masked = rev ? (part * 32 + 31) / R < (quad * 16) / R : (part * 32) / R > (quad * 16 + 15) / R;
-        uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
-        if (!all_masked) {
-          uint32_t r16[16];
-          M3_TMEM_LD16X2(tmem + lane_base + colS + part * 32, r16);
-          tmem_wait_ld();
-          const float di = sc[kPDiag + ti];
-          const float ci = sc[kPCumL2 + ti];
-          uint32_t w[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float vals[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int tk = spos((c0 + 2 * e + u) / R);
-              const float sv = __uint_as_float(r16[2 * e + u]);
-              float wv;
-              if (tk < ti) wv = fact ? sv : sv * ex2_approx(ci - sc[kPCumL2 + tk]);
-              else if (tk == ti) wv = c0 + 2 * e + u == i ? fmaf(sv, di, Dh) : sv * di;  // D v via the diagonal
-              else wv = 0.0f;
-              vals[u] = wv;
-            }
-            w[e] = pack2<T>(vals[0], vals[1]);
-          }
-          w0 = make_uint4(w[0], w[1], w[2], w[3]);
-          w1 = make_uint4(w[4], w[5], w[6], w[7]);
-        }
-        *reinterpret_cast<uint4*>(smem + Lay::W + swz(i, c0, kRows)) = w0;
-        *reinterpret_cast<uint4*>(smem + Lay::W + swz(i, c0 + 8, kRows)) = w1;
-      }
-      fence_async_smem();
-      fence_before();
-      group_bar(kBarE);
-      M3_MARK(1);
-      // ---- MMA 2: intra = W V, into the scores' columns ----
-      if (gt == 0) {
-        fence_after();
-        const uint32_t vb = sbase + v_off(t);
-#pragma unroll
-        for (int kk = 0; kk < kRows / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-          mma_f16(tmem + colS, sdesc(sbase + Lay::W + koff, 16, 1024), sdesc(vb + kk * 2048, kRows * 128, 1024),
-                  id_nmn, kk > 0);
-        }
-        mma_commit(bar_mma2 + 8 * (t & 1));
-      }
-      M3_MARK(2);
-      // z of this thread's epilogue row, fetched while the next tile is launched
-      uint4 zreg[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-      {
-        const int ti = spos((quad * 16 + (lane & 15)) / R);
-        if (ti < nt) {
-          const int tt = scan_token(a, t0 + ti);
-          const uint4* zsrc = reinterpret_cast<const uint4*>(
-              zp + b * a.gate.stride[0] + (int64_t)tt * a.gate.stride[1] + h * a.gate.stride[2] +
-              part * 32 + (lane >> 4) * 16);
-          zreg[0] = zsrc[0];
-          zreg[1] = zsrc[1];
-        }
-      }
-      // ---- the next tile: snapshot and MMA group 1 ----
-      if (t + 1 < ntiles) launch_tile(t + 1, mark);
-      M3_MARK(4);
-      gwait(bar_mma2 + 8 * (t & 1), (t >> 1) & 1, kBarE);
-      fence_after();
-      M3_MARK(5);
-      // ---- epilogue: thread row quad * 16 + (lane & 15), output columns p0 .. p0 + 15 ----
-      {
-        const int i = quad * 16 + (lane & 15);
-        const int ts_ = i / R, r = i % R;
-        const int ti = spos(ts_);
-        const int p0 = part * 32 + (lane >> 4) * 16;
-        uint32_t ra[16], ri[16];
-        M3_TMEM_LD16X2(tmem + lane_base + colS + part * 32, ra);
-        M3_TMEM_LD16X2(tmem + lane_base + colI + part * 32, ri);
-        tmem_wait_ld();
-        const bool valid = ti < nt;
-        const float gi = sc[kPEcum + ti];
-        float out[16];
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t zw[4] = {zreg[c].x, zreg[c].y, zreg[c].z, zreg[c].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int jj = 8 * c + 2 * e;
-            const float y0 = fmaf(gi, __uint_as_float(ri[jj]), __uint_as_float(ra[jj]));
-            const float y1 = fmaf(gi, __uint_as_float(ri[jj + 1]), __uint_as_float(ra[jj + 1]));
-            if (R == 1) {
-              const float2 gz = unpack2<T>(silu2<T>(zw[e]));
-              out[jj] = y0 * gz.x;
-              out[jj + 1] = y1 * gz.y;
-            } else {
-              const float2 z = unpack2<T>(zw[e]);
-              const int p = p0 + jj;
-              const float za = z.x * fsm[Lay::CMz + r * kP + p], zb = z.y * fsm[Lay::CMz + r * kP + p + 1];
-              out[jj] = y0 * __fdividef(za, 1.0f + __expf(-za)) * fsm[Lay::CMo + r * kP + p];
-              out[jj + 1] = y1 * __fdividef(zb, 1.0f + __expf(-zb)) * fsm[Lay::CMo + r * kP + p + 1];
-            }
-          }
-        }
-        if (R > 1) {
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-#pragma unroll
-            for (int o = 1; o < R; o <<= 1) out[jj] += __shfl_xor_sync(0xffffffffu, out[jj], o);
-          }
-        }
-        if (valid && r == 0) {
-          const int tt = scan_token(a, t0 + ti);
-          const int64_t ob = b * a.y.stride[0] + (int64_t)tt * a.y.stride[1] + h * a.y.stride[2] +
-                             (int64_t)p0 * a.y.stride[3];
-          if (vec_y) {
-            uint4* dst = reinterpret_cast<uint4*>(yp + ob);
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-              dst[c] = make_uint4(pack2<T>(out[8 * c], out[8 * c + 1]), pack2<T>(out[8 * c + 2], out[8 * c + 3]),
-                                  pack2<T>(out[8 * c + 4], out[8 * c + 5]), pack2<T>(out[8 * c + 6], out[8 * c + 7]));
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) yp[ob + jj * a.y.stride[3]] = from_f<T>(out[jj]);
-          }
-        }
-      }
-      fence_before();
-      const bool stop = group_bar_or(kBarE, *abort_flag != 0);
-      M3_MARK(6);
-      if (stop) break;
+      mma_commit(bar_addr);
     }
-    M3_MARK_FLUSH;
-    // ---- final state: S[p][n] = phi X^T ----
+    // While the tensor cores run: the next tile's scalars, workspace rows and z rows (other buffer).
+    if (ntn > 0) {
+      fetch_scalars(t0n, ntn);
+      fetch_small(t0n, ntn);
+      issue_z(t0n, ntn, (tile + 1) & 1);
+    }
+    // One thread polls the barrier; the others wait at __syncthreads without taking issue slots.
+    if (tid == 0 && !mbar_wait(bar_addr, phase_bit)) *abort_flag = 1;
+    phase_bit ^= 1;
+    __syncthreads();
     fence_after();
-    if (!*abort_flag) {
-      uint32_t r32[32];
-      M3_TMEM_LD32(tmem + lane_base + kPColX + part * 32, r32);
+    // Q'/K' are free now: the next tile's raw q/k rows.
+    if (ntn > 0) issue_qk(t0n, ntn);
+    M3_MARK(6);
+
+    // ---- W = scores o decay -> smem (16-bit, K-major). Thread: row quad * 16 + (lane & 15), columns
+    // c0 .. c0 + 15 with c0 = part * 32 + (lane >> 4) * 16. ----
+    {
+      const int i = quad * 16 + (lane & 15);
+      const int ti = min(i / R, TOK - 1);
+      const int c0 = part * 32 + (lane >> 4) * 16;
+      const bool all_masked = (part * 32) / R > (quad * 16 + 15) / R;  // warp-uniform
+      uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
+      if (!all_masked) {
+        uint32_t r16[16];
+        M3_TMEM_LD16X2(tmem + lane_base + kColScores + part * 32, r16);
+        tmem_wait_ld();
+        const float di = diag[ti];
+        const float ci = cum_l2[ti];
+        // Branch-free: below the row token's block the score (times the exact decay when the tile is not
+        // factorised), on it gamma / scale (plus D on the diagonal itself: the D v term), above it 0.
+        float f[16];
+        if (fact) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) f[k] = 1.0f;
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) f[k] = ex2_approx(ci - cum_l2[(c0 + k) / R]);
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float vals[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = c0 + 2 * e + u, tk = col / R, ti_ = i / R;
+            const float sv = __uint_as_float(r16[2 * e + u]);
+            const float same = fmaf(sv, di, col == i ? Dh : 0.0f);
+            vals[u] = tk < ti_ ? sv * f[2 * e + u] : (tk == ti_ ? same : 0.0f);
+          }
+          w[e] = pack2<T>(vals[0], vals[1]);
+        }
+        w0 = make_uint4(w[0], w[1], w[2], w[3]);
+        w1 = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+      *reinterpret_cast<uint4*>(smem + kOffW + swz(i, c0, kRows)) = w0;
+      *reinterpret_cast<uint4*>(smem + kOffW + swz(i, c0 + 8, kRows)) = w1;
+    }
+    fence_async_smem();
+    fence_before();
+    __syncthreads();
+    M3_MARK(7);
+
+    // ---- MMA group 2: intra = W V ----
+    if (tid == 0) {
+      fence_after();
+#pragma unroll
+      for (int kk = 0; kk < kRows / 16; ++kk) {
+        const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+        mma_f16(tmem + kColIntra, sdesc(sbase + kOffW + koff, 16, 1024),
+                sdesc(sbase + kOffV + kk * 2048, kRows * 128, 1024), id_nmn, kk > 0);
+      }
+      mma_commit(bar_addr);
+    }
+    if (tid == 0 && !mbar_wait(bar_addr, phase_bit)) *abort_flag = 1;
+    phase_bit ^= 1;
+    __syncthreads();
+    fence_after();
+    // W is free now: the next tile's raw x rows.
+    if (ntn > 0) issue_x(t0n, ntn);
+    cp_async_commit();
+    M3_MARK(8);
+
+    // ---- epilogue: thread row quad * 16 + (lane & 15), output columns p0 .. p0 + 15 ----
+    {
+      const int i = quad * 16 + (lane & 15);
+      const int ti = i / R, r = i % R;
+      const int tc = min(ti, TOK - 1);
+      const int p0 = part * 32 + (lane >> 4) * 16;
+      const uint32_t zoff = kOffZ + (tile & 1) * (kRows * kP * 2);
+      uint32_t ra[16], ri[16];
+      M3_TMEM_LD16X2(tmem + lane_base + kColIntra + part * 32, ra);
+      M3_TMEM_LD16X2(tmem + lane_base + kColInter + part * 32, ri);
       tmem_wait_ld();
-      const int n = quad * 32 + lane;
-      const m3_tensor& fs = a.final_state;
-      float* fsp = static_cast<float*>(fs.data) + b * fs.stride[0] + h * fs.stride[1] + n * fs.stride[3];
+      const bool valid = ti < nt;
+      const float gi = ecum[tc];
+      float out[16];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) fsp[(part * 32 + j) * fs.stride[2]] = __uint_as_float(r32[j]) * phi;
-    }
-  } else if (group == 1) {
-    // =========================== stage group ===========================
-    const bool has_norm = a.q_norm_w.data != nullptr;
-    const bool has_bias = a.q_bias.data != nullptr;
-    M3_MARK_INIT;
-    for (int u = 0; u < ntiles; ++u) {
-      const int t0 = u * TOK, nt = min(TOK, L - t0);
-      float* sc = scal(u);
-      float* wsb = wslot(u);
-      gwait(ring(bar_prep, u), ring_par(u), kBarS);
-      const bool fact = sc[kPMode + 2] != 0.0f;
-      M3_MARK(16);
-      // ---- stage Q', K' in place (packed 16-bit math): q' = rot(q rq w + b) fq, k' = rot(k rk w + b) fk.
-      // Lane: row gw * 8 + 4 it + (lane >> 3), 16-byte chunks c = lane & 7 and c + 8 (elements 8 c ..,
-      // 64 + 8 c ..), so the rotated chunks (the first S pairs; MIMO: n < 32 with n + 64) spread over all
-      // lanes and a MIMO pair never leaves its lane. ----
-      const uint32_t qko = qk_off(u);
-      const int c = lane & 7;
+      for (int c = 0; c < 2; ++c) {
+        const uint4 zz = *reinterpret_cast<const uint4*>(smem + zoff + swz(tc, p0 + 8 * c, kRows));
+        const uint32_t zw[4] = {zz.x, zz.y, zz.z, zz.w};
 #pragma unroll
-      for (int it = 0; it < 2; ++it) {
-        const int row = gw * 8 + 4 * it + (lane >> 3);
-        const int ts_ = row / R, r = row % R;
-        const int j = spos(ts_);
-        const bool valid = j < nt;
-        const float* wrow = wsb + ts_ * WS;
-        const uint32_t off0 = qko + swz(row, 8 * c, kRows), off1 = qko + swz(row, 64 + 8 * c, kRows);
-        uint32_t qv[8], kv[8];
-        {
-          const uint4 q0 = *reinterpret_cast<const uint4*>(smem + off0);
-          const uint4 q1 = *reinterpret_cast<const uint4*>(smem + off1);
-          const uint4 k0 = *reinterpret_cast<const uint4*>(smem + off0 + kRows * kN * 2);
-          const uint4 k1 = *reinterpret_cast<const uint4*>(smem + off1 + kRows * kN * 2);
-          qv[0] = q0.x; qv[1] = q0.y; qv[2] = q0.z; qv[3] = q0.w;
-          qv[4] = q1.x; qv[5] = q1.y; qv[6] = q1.z; qv[7] = q1.w;
-          kv[0] = k0.x; kv[1] = k0.y; kv[2] = k0.z; kv[3] = k0.w;
-          kv[4] = k1.x; kv[5] = k1.y; kv[6] = k1.z; kv[7] = k1.w;
-        }
-#ifdef M3_X_NOSTAGE
-        if (true) continue;
-#endif
-        if (has_norm || has_bias) {
-#pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            const int wo = 4 * c + 32 * hf;  // first packed word of this chunk
-            const uint4 bq = *reinterpret_cast<const uint4*>(cbq + r * (kN / 2) + wo);
-            const uint4 bk = *reinterpret_cast<const uint4*>(cbk + r * (kN / 2) + wo);
-            const uint32_t bqa[4] = {bq.x, bq.y, bq.z, bq.w}, bka[4] = {bk.x, bk.y, bk.z, bk.w};
-            if (has_norm) {
-              const uint32_t rq2 = bcast2<T>(wrow[r]), rk2 = bcast2<T>(wrow[R + r]);
-              const uint4 wq = *reinterpret_cast<const uint4*>(cwq + wo);
-              const uint4 wk = *reinterpret_cast<const uint4*>(cwk + wo);
-              const uint32_t wqa[4] = {wq.x, wq.y, wq.z, wq.w}, wka[4] = {wk.x, wk.y, wk.z, wk.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                qv[4 * hf + e] = fma2<T>(mul2<T>(qv[4 * hf + e], rq2), wqa[e], bqa[e]);
-                kv[4 * hf + e] = fma2<T>(mul2<T>(kv[4 * hf + e], rk2), wka[e], bka[e]);
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                qv[4 * hf + e] = add2<T>(qv[4 * hf + e], bqa[e]);
-                kv[4 * hf + e] = add2<T>(kv[4 * hf + e], bka[e]);
-              }
-            }
-          }
-        }
-#ifndef M3_X_NOROT
-        if (has_phase) {
-#else
-        if (false) {
-#endif
-          const uint32_t* rw = reinterpret_cast<const uint32_t*>(wrow + WA);
-          if (a.mimo_rotation) {
-            // pairs (n, n + 64) for n < 32: chunk c < 4 and chunk c + 8 of the same lane
-            if (c < 4) {
-              const uint4 c4 = *reinterpret_cast<const uint4*>(rw + 4 * c);
-              const uint4 s4 = *reinterpret_cast<const uint4*>(rw + 16 + 4 * c);
-              const uint32_t ca[4] = {c4.x, c4.y, c4.z, c4.w}, sa[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const uint32_t ns = sa[e] ^ 0x80008000u;
-                const uint32_t qa_ = qv[e], qb_ = qv[4 + e], ka_ = kv[e], kb_ = kv[4 + e];
-                qv[e] = fma2<T>(qb_, ns, mul2<T>(qa_, ca[e]));         // a c - b s
-                qv[4 + e] = fma2<T>(qa_, sa[e], mul2<T>(qb_, ca[e]));  // a s + b c
-                kv[e] = fma2<T>(kb_, ns, mul2<T>(ka_, ca[e]));
-                kv[4 + e] = fma2<T>(ka_, sa[e], mul2<T>(kb_, ca[e]));
-              }
-            }
-          } else if (4 * c < S) {
-            // adjacent pairs (2m, 2m + 1), m = 4 c + e, all in the first chunk
-            const uint4 c4 = *reinterpret_cast<const uint4*>(rw + 4 * c);
-            const uint32_t csa[4] = {c4.x, c4.y, c4.z, c4.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              if (4 * c + e < S) {
-                const uint32_t cc = __byte_perm(csa[e], 0, 0x1010);
-                const uint32_t ms = __byte_perm(csa[e], 0, 0x3232) ^ 0x00008000u;
-                qv[e] = rot_pair<T>(qv[e], cc, ms);
-                kv[e] = rot_pair<T>(kv[e], cc, ms);
-              }
-            }
-          }
-        }
-        if (valid && a.final_k.data && t0 + j == L - 1) {
-          const m3_tensor& fkt = a.final_k;
-          T* fkp = static_cast<T*>(fkt.data) + b * fkt.stride[0] + h * fkt.stride[1] + r * fkt.stride[2];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int n = (e < 4 ? 8 * c : 64 + 8 * c) + 2 * (e & 3);
-            fkp[n * fkt.stride[3]] = from_f<T>(lo16<T>(kv[e]));
-            fkp[(n + 1) * fkt.stride[3]] = from_f<T>(hi16<T>(kv[e]));
-          }
-        }
-        // Rows outside the sequence (zero-filled by the TMA) would still carry the bias: zero them.
-        const uint32_t fq2 = valid ? bcast2<T>(sc[kPFq + j]) : 0u, fk2 = valid ? bcast2<T>(sc[kPFk + j]) : 0u;
-        *reinterpret_cast<uint4*>(smem + off0) =
-            make_uint4(mul2<T>(qv[0], fq2), mul2<T>(qv[1], fq2), mul2<T>(qv[2], fq2), mul2<T>(qv[3], fq2));
-        *reinterpret_cast<uint4*>(smem + off1) =
-            make_uint4(mul2<T>(qv[4], fq2), mul2<T>(qv[5], fq2), mul2<T>(qv[6], fq2), mul2<T>(qv[7], fq2));
-        *reinterpret_cast<uint4*>(smem + off0 + kRows * kN * 2) =
-            make_uint4(mul2<T>(kv[0], fk2), mul2<T>(kv[1], fk2), mul2<T>(kv[2], fk2), mul2<T>(kv[3], fk2));
-        *reinterpret_cast<uint4*>(smem + off1 + kRows * kN * 2) =
-            make_uint4(mul2<T>(kv[4], fk2), mul2<T>(kv[5], fk2), mul2<T>(kv[6], fk2), mul2<T>(kv[7], fk2));
-      }
-      // ---- V = x mx_r (R > 1; R = 1 uses the raw rows in place, tokens outside the sequence are zero) ----
-      const uint32_t vo = v_off(u);
-      if (R > 1) {
-        const uint32_t xo = xr_off(u);
-        for (int c = gt; c < kRows * (kP / 8); c += 256) {
-          const int row = c >> 3, ch = c & 7;
-          const int r = row % R;
-          uint4 v4 = *reinterpret_cast<const uint4*>(smem + xo + swz(row / R, 8 * ch, kRows));
-          const uint4 m4 = *reinterpret_cast<const uint4*>(
-              reinterpret_cast<const uint32_t*>(fsm + Lay::CMxp) + r * (kP / 2) + 4 * ch);
-          v4 = make_uint4(mul2<T>(v4.x, m4.x), mul2<T>(v4.y, m4.y), mul2<T>(v4.z, m4.z), mul2<T>(v4.w, m4.w));
-          *reinterpret_cast<uint4*>(smem + vo + swz(row, 8 * ch, kRows)) = v4;
-        }
-      }
-      if (!fact) {
-        // V2 = V e^{cum_last - cum}; V2 was last read by MMA group 1 of the previous tile.
-        if (u > 0) gwait(bar_mma1 + 8 * ((u - 1) & 1), ((u - 1) >> 1) & 1, kBarS);
-        else group_bar(kBarS);
-        for (int c = gt; c < kRows * (kP / 8); c += 256) {
-          const int row = c >> 3, ch = c & 7;
-          const int jc = min(spos(row / R), TOK - 1);
-          const uint4 v4 = *reinterpret_cast<const uint4*>(smem + vo + swz(row, 8 * ch, kRows));
-          const uint32_t e2 = bcast2<T>(sc[kPEdec + jc]);
-          *reinterpret_cast<uint4*>(smem + Lay::V2 + swz(row, 8 * ch, kRows)) =
-              make_uint4(mul2<T>(v4.x, e2), mul2<T>(v4.y, e2), mul2<T>(v4.z, e2), mul2<T>(v4.w, e2));
-        }
-      }
-      fence_async_smem();
-      fence_before();
-      const bool stop = group_bar_or(kBarS, *abort_flag != 0);
-      M3_MARK(17);
-      if (gt == 0) mbar_arrive(ring(bar_staged, u));
-      if (stop) break;
-    }
-    M3_MARK_FLUSH;
-  } else {
-    // =========================== prep group ===========================
-    // Warp 0: per-token scalars (two tokens per lane, lane 0 also the first token after the tile).
-    // Warps 1-8: phases; warp 1 + g owns angles 4 g .. 4 g + 3, whose carried block offset and
-    // in-block sum (mamba3/model.py:246-251) stay in registers across tiles.
-    const int pw = warp - 16;
-    const int s0 = 4 * (pw - 1);
-    float ph_off[4], ph_loc[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      ph_off[k] = (pw > 0 && a.initial_phase.data && s0 + k < S)
-                      ? ld_t(a.initial_phase, b * a.initial_phase.stride[0] + h * a.initial_phase.stride[1] +
-                                                  (s0 + k) * a.initial_phase.stride[2])
-                      : 0.0f;
-      ph_loc[k] = 0.0f;
-    }
-    // Raw scalar words of tokens 2 lane, 2 lane + 1 (and of the next tile's first token in lane 0),
-    // fetched a tile ahead by warp 0.
-    uint32_t rd[2] = {0, 0}, ra[2] = {0, 0}, rt[2] = {0, 0}, rnd = 0, rnt = 0;
-    bool rok[2] = {false, false}, rnok = false;
-    auto fetch_scalars = [&](int u) {
-      const int t0n = u * TOK, ntn = min(TOK, L - t0n);
-#pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        const int j = 2 * lane + m;
-        rok[m] = j < ntn;
-        if (rok[m]) {
-          const int t = scan_token(a, t0n + j);
-          rd[m] = raw_word(a.dt, b * a.dt.stride[0] + (int64_t)t * a.dt.stride[1] + h * a.dt.stride[2]);
-          ra[m] = raw_word(a.adt, b * a.adt.stride[0] + (int64_t)t * a.adt.stride[1] + h * a.adt.stride[2]);
-          rt[m] = raw_word(a.trap, b * a.trap.stride[0] + (int64_t)t * a.trap.stride[1] + h * a.trap.stride[2]);
-        }
-      }
-      rnok = lane == 0 && ntn == TOK && t0n + TOK < L;
-      if (rnok) {
-        const int t = scan_token(a, t0n + TOK);
-        rnd = raw_word(a.dt, b * a.dt.stride[0] + (int64_t)t * a.dt.stride[1] + h * a.dt.stride[2]);
-        rnt = raw_word(a.trap, b * a.trap.stride[0] + (int64_t)t * a.trap.stride[1] + h * a.trap.stride[2]);
-      }
-    };
-    // mamba3/model.py:195-198: dt = softplus(delta + dt_bias); A = -heavytail(a) clamped <= -1e-4.
-    auto to_dt = [&](uint32_t w) {
-      const float x = word_to_f(w, a.dt.dtype);
-      return a.dt_bias.data ? softplusf_(x + dt_bias_h) : x;
-    };
-    if (gt == 0) tma_tile(0);
-    fill_tile(0);
-    if (pw == 0) fetch_scalars(0);
-    M3_MARK_INIT;
-    for (int u = 0; u < ntiles; ++u) {
-      const int t0 = u * TOK, nt = min(TOK, L - t0);
-      float* sc = scal(u);
-      float* wsb = wslot(u);
-      M3_MARK(23);
-      // ---- loads of tile u + 1 into the slots of tile u - 2 ----
-      if (u + 1 < ntiles) {
-        if (gt == 0) {
-          bool ok = true;
-          if (u >= 2) {
-            // Q'/K' and workspace slots are free once MMA group 1 of tile u - 2 has run, the V slot
-            // once MMA 2 has; the epilogue of tile u - 3 (last reader of the scalar slot) came before.
-            ok = mbar_wait(bar_mma1 + 8 * ((u - 2) & 1), ((u - 2) >> 1) & 1);
-            if (ok) ok = mbar_wait(bar_mma2 + 8 * ((u - 2) & 1), ((u - 2) >> 1) & 1);
-          }
-          if (ok) tma_tile(u + 1);
-          else *abort_flag = 1;
-        }
-        group_bar_n(kBarP, kPrepThreads);
-        fill_tile(u + 1);
-      }
-      M3_MARK(21);
-      // ---- warp 0: dt, adt, sigma of the tile's tokens (dt also to smem for the phase warps) ----
-      float dtv[2] = {0.0f, 0.0f}, adv[2] = {0.0f, 0.0f}, sgv[2] = {0.0f, 0.0f}, nbeta = 0.0f;
-      if (pw == 0) {
-#pragma unroll
-        for (int m = 0; m < 2; ++m) {
-          if (rok[m]) {
-            dtv[m] = to_dt(rd[m]);
-            const float araw = word_to_f(ra[m], a.adt.dtype);
-            adv[m] = a.dt_bias.data ? fminf(-heavy_tailf(araw), -kAFloor) * dtv[m] : araw;
-            sgv[m] = sigmoidf_(word_to_f(rt[m], a.trap.dtype));
-          }
-        }
-        if (rnok) nbeta = to_dt(rnd) * (1.0f - sigmoidf_(word_to_f(rnt, a.trap.dtype)));
-        if (2 * lane < TOK) *reinterpret_cast<float2*>(sdt + 2 * lane) = make_float2(dtv[0], dtv[1]);
-        if (u + 1 < ntiles) fetch_scalars(u + 1);
-      }
-      // this tile's rows (issued a tile ago) have landed
-      if (gt == 0 && !mbar_wait(ring(bar_tma, u), ring_par(u))) *abort_flag = 1;
-      group_bar_n(kBarP, kPrepThreads);
-      M3_MARK(22);
-      if (pw == 0) {
-        // ---- cumulative decay, trapezoid scale, decay factorisation (mamba3/ops.py:659-671) ----
-        const float incl = warp_incl_scan(adv[0] + adv[1], lane);
-        const float cum2[2] = {incl - adv[1], incl};  // tokens 2 lane, 2 lane + 1
-        const int jm = (nt - 1) >> 1, jl = nt - 1;
-        const float cmid = __shfl_sync(0xffffffffu, (jm & 1) ? cum2[1] : cum2[0], jm >> 1);
-        const float cl = __shfl_sync(0xffffffffu, (jl & 1) ? cum2[1] : cum2[0], jl >> 1);
-        // scale_j = gamma_j + dt_{j+1} (1 - sigma_{j+1}) (the token after the tile for the last one)
-        const float beta0 = dtv[0] * (1.0f - sgv[0]);
-        const float beta_up = __shfl_down_sync(0xffffffffu, beta0, 1);
-        const float beta_next = __shfl_sync(0xffffffffu, nbeta, 0);
-        const int j0 = 2 * lane;
-        const float nx[2] = {j0 + 1 < nt ? dtv[1] * (1.0f - sgv[1]) : 0.0f,
-                             j0 + 2 < nt ? beta_up : ((j0 + 2 == TOK && nt == TOK) ? beta_next : 0.0f)};
-        float scv[2], dg[2], dev = 0.0f;
-#pragma unroll
-        for (int m = 0; m < 2; ++m) {
-          const bool v = j0 + m < nt;
-          const float gamma = dtv[m] * sgv[m];
-          scv[m] = v ? gamma + nx[m] : 0.0f;
-          dg[m] = v ? gamma / scv[m] : 0.0f;
-          if (v) dev = fmaxf(dev, fabsf(cum2[m] - cmid));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) dev = fmaxf(dev, __shfl_xor_sync(0xffffffffu, dev, o));
-        const bool fct = dev <= kLim;
-        if (j0 < TOK) {
-          float o_cl[2], o_fq[2], o_fk[2], o_ec[2], o_ed[2];
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            const bool v = j0 + m < nt;
-            const float c = cum2[m];
-            o_cl[m] = c * kLog2e;
-            o_fq[m] = v ? (fct ? __expf(c - cmid) : 1.0f) : 0.0f;
-            o_fk[m] = v ? (fct ? scv[m] * __expf(cmid - c) : scv[m]) : 0.0f;
-            o_ec[m] = v ? (fct ? __expf(cmid) : __expf(c)) : 0.0f;
-            o_ed[m] = (v && !fct) ? __expf(cl - c) : 0.0f;
-          }
-          *reinterpret_cast<float2*>(sc + kPCumL2 + j0) = make_float2(o_cl[0], o_cl[1]);
-          *reinterpret_cast<float2*>(sc + kPDiag + j0) = make_float2(dg[0], dg[1]);
-          *reinterpret_cast<float2*>(sc + kPFq + j0) = make_float2(o_fq[0], o_fq[1]);
-          *reinterpret_cast<float2*>(sc + kPFk + j0) = make_float2(o_fk[0], o_fk[1]);
-          *reinterpret_cast<float2*>(sc + kPEcum + j0) = make_float2(o_ec[0], o_ec[1]);
-          *reinterpret_cast<float2*>(sc + kPEdec + j0) = make_float2(o_ed[0], o_ed[1]);
-        }
-        if (lane == 0) {
-          sc[kPMode] = cmid;
-          sc[kPMode + 1] = cl;
-          sc[kPMode + 2] = fct ? 1.0f : 0.0f;
-          sc[kPMode + 3] = __expf(cl);
-        }
-      } else if (has_phase) {
-        // ---- phases -> packed (cos, sin) words over pi*tanh(angle) in the workspace rows. Lane:
-        // scan positions 2 lane, 2 lane + 1; SISO: word m = (cos_m, sin_m); MIMO (S == 32): word q < 16 =
-        // (cos_2q, cos_2q+1), word 16 + q = (sin_2q, sin_2q+1), the element pairs a staging word holds. ----
-        const int j0 = 2 * lane;
-        float ph[2][4];
-        if (s0 < S) {
-          if (a.angles.data) {
-            if (t0 > 0 && (t0 % kPhaseBlock) == 0) {
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                ph_off[k] = fmodf(ph_off[k] + ph_loc[k], kTwoPi);
-                ph_loc[k] = 0.0f;
-              }
-            }
-            float inc[2][4];
-#pragma unroll
-            for (int m = 0; m < 2; ++m) {
-              const int j = j0 + m;
-              float4 av = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-              float dtj = 0.0f;
-              if (j < nt) {
-                av = *reinterpret_cast<const float4*>(wsb + spos(j) * WS + WA + s0);
-                dtj = sdt[j];
-              }
-              const float in[4] = {av.x, av.y, av.z, av.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) inc[m][k] = s0 + k < S ? fmod_2pi(in[k] * dtj) : 0.0f;
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float x = warp_incl_scan(inc[0][k] + inc[1][k], lane);
-              const float tot = __shfl_sync(0xffffffffu, x, 31);
-              ph[0][k] = fmod_2pi((ph_loc[k] + (x - inc[1][k])) + ph_off[k]);
-              ph[1][k] = fmod_2pi((ph_loc[k] + x) + ph_off[k]);
-              ph_loc[k] += tot;
-            }
+        for (int e = 0; e < 4; ++e) {
+          const int jj = 8 * c + 2 * e;
+          // D v arrives through the diagonal of W (intra)
+          const float y0 = fmaf(gi, __uint_as_float(ri[jj]), __uint_as_float(ra[jj]));
+          const float y1 = fmaf(gi, __uint_as_float(ri[jj + 1]), __uint_as_float(ra[jj + 1]));
+          if (R == 1) {
+            const float2 g = unpack2<T>(silu2<T>(zw[e]));
+            out[jj] = y0 * g.x;
+            out[jj + 1] = y1 * g.y;
           } else {
-#pragma unroll
-            for (int m = 0; m < 2; ++m) {
-              const int j = j0 + m;
-              float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-              if (j < TOK) pv = *reinterpret_cast<const float4*>(wsb + spos(j) * WS + WA + s0);
-              ph[m][0] = pv.x;
-              ph[m][1] = pv.y;
-              ph[m][2] = pv.z;
-              ph[m][3] = pv.w;
-            }
-          }
-        }
-        if (a.mimo_rotation) named_bar(kBarPhase, 256);  // MIMO words land on other warps' angle slots
-        if (s0 < S) {
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            const int j = j0 + m;
-            if (j < TOK) {
-              float cs[4], sn[4];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) __sincosf(ph[m][k], &sn[k], &cs[k]);  // |phase| < 2 pi
-              if (t0 + j == L - 1 && a.final_phase.data) {
-                const m3_tensor& fp = a.final_phase;
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                  if (s0 + k < S)
-                    static_cast<float*>(fp.data)[b * fp.stride[0] + h * fp.stride[1] + (s0 + k) * fp.stride[2]] =
-                        ph[m][k];
-              }
-              uint32_t* w = reinterpret_cast<uint32_t*>(wsb + spos(j) * WS + WA);
-              if (a.mimo_rotation) {
-                *reinterpret_cast<uint2*>(w + s0 / 2) = make_uint2(pack2<T>(cs[0], cs[1]), pack2<T>(cs[2], cs[3]));
-                *reinterpret_cast<uint2*>(w + 16 + s0 / 2) = make_uint2(pack2<T>(sn[0], sn[1]), pack2<T>(sn[2], sn[3]));
-              } else if (s0 + 4 <= S) {
-                *reinterpret_cast<uint4*>(w + s0) = make_uint4(pack2<T>(cs[0], sn[0]), pack2<T>(cs[1], sn[1]),
-                                                               pack2<T>(cs[2], sn[2]), pack2<T>(cs[3], sn[3]));
-              } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                  if (s0 + k < S) w[s0 + k] = pack2<T>(cs[k], sn[k]);
-              }
-            }
+            const float2 z = unpack2<T>(zw[e]);
+            const int p = p0 + jj;
+            const float za = z.x * cst[Lay::CMz + r * kP + p], zb = z.y * cst[Lay::CMz + r * kP + p + 1];
+            out[jj] = y0 * __fdividef(za, 1.0f + __expf(-za)) * cst[Lay::CMo + r * kP + p];
+            out[jj + 1] = y1 * __fdividef(zb, 1.0f + __expf(-zb)) * cst[Lay::CMo + r * kP + p + 1];
           }
         }
       }
-      M3_MARK(24);
-      const bool stop = group_bar_or_n(kBarP, kPrepThreads, *abort_flag != 0);
-      M3_MARK(18);
-      if (gt == 0) mbar_arrive(ring(bar_prep, u));
-      if (stop) break;
+      if (R > 1) {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+#pragma unroll
+          for (int o = 1; o < R; o <<= 1) out[jj] += __shfl_xor_sync(0xffffffffu, out[jj], o);
+        }
+      }
+      if (valid && r == 0) {
+        const int t = scan_token(a, t0 + ti);
+        const int64_t ob = b * a.y.stride[0] + (int64_t)t * a.y.stride[1] + h * a.y.stride[2] +
+                           (int64_t)p0 * a.y.stride[3];
+        if (vec_y) {
+          uint4* dst = reinterpret_cast<uint4*>(yp + ob);
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            dst[c] = make_uint4(pack2<T>(out[8 * c], out[8 * c + 1]), pack2<T>(out[8 * c + 2], out[8 * c + 3]),
+                                pack2<T>(out[8 * c + 4], out[8 * c + 5]), pack2<T>(out[8 * c + 6], out[8 * c + 7]));
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) yp[ob + jj * a.y.stride[3]] = from_f<T>(out[jj]);
+        }
+      }
     }
-    M3_MARK_FLUSH;
+    M3_MARK(9);
+    if (ntn > 0) finish_scalars();  // the next tile's scalars, loaded during the first MMA group
+    fence_before();
+    __syncthreads();
+    M3_MARK(10);
+    if (*abort_flag) break;
+  }
+  cp_async_wait_all();
+
+  // ---- final state: S[p][n] = phi X^T ----
+  fence_after();
+  if (!*abort_flag) {
+    uint32_t r32[32];
+    M3_TMEM_LD32(tmem + lane_base + kColState + part * 32, r32);
+    tmem_wait_ld();
+    const int n = quad * 32 + lane;
+    const m3_tensor& fs = a.final_state;
+    float* fsp = static_cast<float*>(fs.data) + b * fs.stride[0] + h * fs.stride[1] + n * fs.stride[3];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) fsp[(part * 32 + j) * fs.stride[2]] = __uint_as_float(r32[j]) * phi;
   }
   fence_before();
   __syncthreads();
   if (warp == 0) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPTmemCols));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
 static bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against the driver).
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// 16-bit row tiles: dims / element strides innermost first (strides of dims 1.. only).
-static bool encode_rows(CUtensorMap* map, const m3_tensor& t, int rank, const uint64_t* dims, const int64_t* strides,
-                        const uint32_t* box) {
-  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
-  if (enc == nullptr) return false;
-  cuuint64_t gdim[5], gstr[4];
-  cuuint32_t bdim[5], estr[5];
-  for (int i = 0; i < rank; ++i) {
-    gdim[i] = dims[i];
-    bdim[i] = box[i];
-    estr[i] = 1;
-  }
-  // A dimension of extent 1 is only ever read at coordinate 0: give it a valid nonzero stride.
-  for (int i = 0; i + 1 < rank; ++i) gstr[i] = (cuuint64_t)(dims[i + 1] == 1 ? 8 : strides[i]) * 2;
-  const CUtensorMapDataType dt = t.dtype == M3_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  return enc(map, dt, (cuuint32_t)rank, t.data, gdim, gstr, bdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-         CUDA_SUCCESS;
-}
 
 template <typename T, int R>
 static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
@@ -1382,39 +1152,11 @@ static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
     cudaError_t pe = cudaGetLastError();
     if (pe != cudaSuccess) return pe;
   }
-  constexpr uint32_t TOK = PLayout<R>::TOK;
-  TileMaps tm;
-  memset(&tm, 0, sizeof(tm));
-  {
-    const uint64_t dq[5] = {(uint64_t)a.d_state, (uint64_t)R, (uint64_t)a.groups, (uint64_t)a.length,
-                            (uint64_t)a.batch};
-    const uint32_t bq[5] = {64, (uint32_t)R, 1, TOK, 1};
-    const int64_t sq[4] = {a.q.stride[3], a.q.stride[2], a.q.stride[1], a.q.stride[0]};
-    const int64_t sk[4] = {a.k.stride[3], a.k.stride[2], a.k.stride[1], a.k.stride[0]};
-    const uint64_t dx[4] = {(uint64_t)a.head_dim, (uint64_t)a.heads, (uint64_t)a.length, (uint64_t)a.batch};
-    const uint32_t bx[4] = {64, 1, TOK, 1};
-    const int64_t sx[3] = {a.value.stride[2], a.value.stride[1], a.value.stride[0]};
-    if (!encode_rows(&tm.q, a.q, 5, dq, sq, bq) || !encode_rows(&tm.k, a.k, 5, dq, sk, bq) ||
-        !encode_rows(&tm.x, a.value, 4, dx, sx, bx))
-      return cudaErrorInvalidValue;
-  }
-  if (a.workspace.data) {
-    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
-    const int W = ws_stride(R, a.num_angles);
-    const cuuint64_t gdim[3] = {(cuuint64_t)W, (cuuint64_t)a.length, (cuuint64_t)a.batch};
-    const cuuint64_t gstr[2] = {(cuuint64_t)W * 4, (cuuint64_t)a.length * W * 4};
-    const cuuint32_t bdim[3] = {(cuuint32_t)W, TOK, 1}, estr[3] = {1, 1, 1};
-    if (enc(&tm.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.workspace.data, gdim, gstr, bdim, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return cudaErrorInvalidValue;
-  }
-  auto kern = scan_pipe_kernel<T, R>;
-  constexpr uint32_t smem = PLayout<R>::SmemBytes;
-  static_assert(smem <= 232448, "shared memory map exceeds the per-block limit");
+  auto kern = scan_umma_kernel<T, R>;
+  constexpr uint32_t smem = Layout<R>::SmemBytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(a.heads, a.batch), kPipeThreads, smem, stream>>>(a, tm, vec_y);
+  kern<<<dim3(a.heads, a.batch), kThreads, smem, stream>>>(a, vec_y);
   return cudaGetLastError();
 }
 
@@ -1441,17 +1183,7 @@ int64_t scan_umma_workspace_bytes(const m3_scan_args& a) {
 static bool rows16(const m3_tensor& t, int nd) {
   if ((reinterpret_cast<uintptr_t>(t.data) & 15u) != 0 || t.stride[nd - 1] != 1) return false;
   for (int i = 0; i < nd - 1; ++i)
-    if (t.stride[i] % 8 != 0 || t.stride[i] < 0) return false;
-  return true;
-}
-
-// Tensor-map strides: every dimension of extent > 1 advances through memory.
-static bool strided(const m3_tensor& t, std::initializer_list<int64_t> extents) {
-  int i = 0;
-  for (int64_t e : extents) {
-    if (e > 1 && t.stride[i] == 0) return false;
-    ++i;
-  }
+    if (t.stride[i] % 8 != 0) return false;
   return true;
 }
 
@@ -1459,8 +1191,6 @@ bool scan_umma_supported(const m3_scan_args& a) {
   const bool has_phase = a.phase.data != nullptr || a.angles.data != nullptr;
   return (a.value.dtype == M3_BF16 || a.value.dtype == M3_F16) && a.d_state == umma::kN &&
          rows16(a.q, 5) && rows16(a.k, 5) && rows16(a.value, 4) && rows16(a.gate, 4) &&
-         strided(a.q, {a.batch, a.length, a.groups, a.rank}) && strided(a.k, {a.batch, a.length, a.groups, a.rank}) &&
-         strided(a.value, {a.batch, a.length, a.heads}) && strided(a.gate, {a.batch, a.length, a.heads}) &&
          !(a.q_norm_w.data != nullptr && a.phase.data != nullptr) &&
          a.head_dim == umma::kP && (a.rank == 1 || a.rank == 2 || a.rank == 4 || a.rank == 8) &&
          (!has_phase || (a.mimo_rotation ? a.num_angles == umma::kMaxAngles : a.num_angles <= umma::kMaxAngles));

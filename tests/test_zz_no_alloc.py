@@ -67,7 +67,7 @@ def test_noalloc_rejects_sizes_beyond_the_fixed_scratch():
     lib.m3_scan_fwd_noalloc.argtypes = [ctypes.POINTER(_ext.ScanArgs), ctypes.c_void_p]
     lib.m3_scan_fwd_noalloc.restype = ctypes.c_int
     args = _ext.ScanArgs()
-    args.batch, args.length, args.groups, args.heads, args.rank = 64, 100_000, 1, 2, 1
+    args.batch, args.length, args.groups, args.heads, args.rank = 64, 100_000, 1, 8, 1
     args.d_state, args.head_dim, args.num_angles, args.chunk_hint, args.device = 128, 64, 32, 256, 0
     # Descriptors only (nothing is launched): aligned, contiguous-row layouts of the shapes above.
     def desc(nd, dtype=_ext.M3_BF16):
@@ -76,6 +76,7 @@ def test_noalloc_rejects_sizes_beyond_the_fixed_scratch():
             t.stride[i] = 1 if i == nd - 1 else 1024
         return t
     args.q, args.k, args.value, args.gate = desc(5), desc(5), desc(4), desc(4)
+    args.dt, args.adt, args.trap = desc(3), desc(3), desc(3)  # per-token scalar columns [B, L, H]
     args.q_norm_w = desc(1, _ext.M3_F32)
     assert lib.m3_scan_workspace_bytes(ctypes.byref(args)) > 8 * 1024 * 1024
     assert lib.m3_scan_fwd_noalloc(ctypes.byref(args), None) == 1  # M3_ERR_SHAPE, nothing launched
