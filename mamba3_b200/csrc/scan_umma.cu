@@ -29,6 +29,13 @@
 //
 // Synchronisation: one mbarrier tracks tcgen05.commit of each MMA group; every wait on it is
 // bounded by %globaltimer (2 s) and sets the library's device error word instead of hanging.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <initializer_list>
+#include <mutex>
+
 #include "scan_common.cuh"
 
 namespace m3 {
@@ -97,7 +104,7 @@ template <int R> struct Layout {
   // CBq/CBk: packed bias words [R][64]; CMx/CMz/CMo: MIMO projections (float); CMxp: CMx packed [R][32]
   static constexpr int CBq = kSEnd, CBk = CBq + R * kN, CMx = CBk + R * kN, CMz = CMx + R * kP, CMo = CMz + R * kP;
   static constexpr int CMxp = CMo + R * kP;
-  static constexpr int Ws = ((CMxp + R * kP / 2 + 3) / 4) * 4;  // tile's workspace rows [TOK][WSP]
+  static constexpr int Ws = ((CMxp + R * kP / 2 + 31) / 32) * 32;  // tile's workspace rows [TOK][WSP] (128 B)
   static constexpr int Seg = Ws + TOK * WSP;            // [kWarps][32] sums, then [kWarps][32] offsets
   static constexpr int Carry = Seg + 2 * kWarps * 32;   // [0..31] block offset, [32..63] within-block sum
   static constexpr int FEnd = Carry + 64;
@@ -219,6 +226,40 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// Tiled TMA loads (no multicast) completing on an mbarrier; coordinates innermost first.
+__device__ __forceinline__ void tma_load5(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load4(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load3(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+
+// Tensor maps of the row tiles: q/k [N, R, G, L, B] and x/z [P, H, L, B] (16-bit, 128-byte swizzle,
+// boxes of 64 columns x one tile of rows), workspace rows [WS, L, B] (float, no swizzle).
+struct alignas(64) TileMaps {
+  CUtensorMap q, k, x, z, ws;
+};
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -345,7 +386,8 @@ __global__ void __launch_bounds__(256) token_prep_kernel(const m3_scan_args a, f
 __device__ __forceinline__ float fmod_2pi(float x) { return x - kTwoPi * truncf(x * (1.0f / kTwoPi)); }
 
 template <typename T, int R>
-__global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_args a, int vec_y) {
+__global__ void __launch_bounds__(kThreads, 2)
+    scan_umma_kernel(const m3_scan_args a, const __grid_constant__ TileMaps tm, int vec_y) {
   using Lay = Layout<R>;
   constexpr int TOK = Lay::TOK;
   constexpr int kRowsPerWarp = kRows / kWarps;               // staging rows per warp (8)
@@ -381,6 +423,10 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Lay::OffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::OffBar + 8);
   int* abort_flag = reinterpret_cast<int*>(smem + Lay::OffBar + 16);
+  // Forward scans load their row tiles with TMA (three boxes groups per tile complete on tma_bar);
+  // reverse scans, whose tiles run backwards through memory, use per-row asynchronous copies.
+  const uint32_t tma_bar = smem_u32(smem + Lay::OffBar + 24);
+  const bool use_tma = !a.reverse;
   const uint32_t bar_addr = smem_u32(bar);
   const uint32_t sbase = smem_u32(smem);
   const bool has_phase = a.phase.data != nullptr || a.angles.data != nullptr;
@@ -404,6 +450,16 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
   // q/k rows go straight into the Q'/K' tiles (processed in place), raw x into the W tile, z into the
   // z tile of the tile's parity, workspace rows into wsb.
   auto issue_qk = [&](int t0n, int ntn) {
+    if (use_tma) {
+      if (tid == 0) {
+        mbar_expect_tx(tma_bar, 4u * (kRows * 64 * 2));
+        tma_load5(sbase + kOffQ, &tm.q, 0, 0, g, t0n, b, tma_bar);
+        tma_load5(sbase + kOffQ + kRows * 128, &tm.q, 64, 0, g, t0n, b, tma_bar);
+        tma_load5(sbase + kOffK, &tm.k, 0, 0, g, t0n, b, tma_bar);
+        tma_load5(sbase + kOffK + kRows * 128, &tm.k, 64, 0, g, t0n, b, tma_bar);
+      }
+      return;
+    }
     constexpr int kQChunks = kRows * (kN / 8);
     for (int c = tid; c < kQChunks; c += kThreads) {
       const int row = c >> 4, c8 = c & 15;
@@ -417,6 +473,13 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
     }
   };
   auto issue_x = [&](int t0n, int ntn) {
+    if (use_tma) {
+      if (tid == 0) {
+        mbar_expect_tx(tma_bar, (uint32_t)(TOK * kP * 2));
+        tma_load4(sbase + kOffW, &tm.x, 0, h, t0n, b, tma_bar);
+      }
+      return;
+    }
     for (int c = tid; c < TOK * (kP / 8); c += kThreads) {
       const int j = c >> 3, c8 = c & 7;
       if (j < ntn) {
@@ -427,6 +490,14 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
   };
   auto issue_z = [&](int t0n, int ntn, int par) {
     const uint32_t zoff = kOffZ + par * (kRows * kP * 2);
+    if (use_tma) {  // the z rows and (with a workspace) the workspace rows of the tile
+      if (tid == 0) {
+        mbar_expect_tx(tma_bar, (uint32_t)(TOK * kP * 2) + (has_ws ? (uint32_t)(TOK * WS * 4) : 0u));
+        tma_load4(sbase + zoff, &tm.z, 0, h, t0n, b, tma_bar);
+        if (has_ws) tma_load3(smem_u32(wsb), &tm.ws, 0, t0n, b, tma_bar);
+      }
+      return;
+    }
     for (int c = tid; c < TOK * (kP / 8); c += kThreads) {
       const int j = c >> 3, c8 = c & 7;
       if (j < ntn) {
@@ -481,7 +552,9 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
   };
   // Workspace rows (cp.async) or their stand-ins, and the phase tensor of the op-level API.
   auto fetch_small = [&](int t0n, int ntn) {
-    if (has_ws) {
+    if (has_ws && use_tma) {
+      // the workspace rows travel with the z rows (issue_z)
+    } else if (has_ws) {
       const int chunks = WS / 4;  // <= 12: one 16-slot row per token, no division
       for (int c = tid; c < TOK * 16; c += kThreads) {
         const int j = c >> 4, c4 = c & 15;
@@ -515,6 +588,7 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
   }
   if (tid == 0) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_addr));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 3;" ::"r"(tma_bar));  // q/k, x, z (+ workspace)
     asm volatile("fence.mbarrier_init.release.cluster;");
     *abort_flag = 0;
   }
@@ -637,12 +711,17 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
                     : 0.0f;
     ph_loc[k] = 0.0f;
   }
+  uint32_t tma_phase = 0;
   int tile = 0;
   for (int t0 = 0; t0 < L; t0 += TOK, ++tile) {
     const int nt = min(TOK, L - t0);
     const int t0n = t0 + TOK, ntn = min(TOK, L - t0n);  // next tile (ntn <= 0: none)
     M3_MARK(0);
     cp_async_wait_all();  // this tile's rows, workspace rows (issued during the previous tile)
+    if (use_tma) {
+      if (tid == 0 && !mbar_wait(tma_bar, tma_phase)) *abort_flag = 1;
+      tma_phase ^= 1;
+    }
     __syncthreads();
     M3_MARK(1);
 
@@ -1140,6 +1219,40 @@ __global__ void __launch_bounds__(kThreads, 2) scan_umma_kernel(const m3_scan_ar
 
 static bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against the driver).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 16-bit row tiles: dims / element strides innermost first (strides of dims 1.. only).
+static bool encode_rows(CUtensorMap* map, const m3_tensor& t, int rank, const uint64_t* dims, const int64_t* strides,
+                        const uint32_t* box) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  cuuint64_t gdim[5], gstr[4];
+  cuuint32_t bdim[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estr[i] = 1;
+  }
+  // A dimension of extent 1 is only ever read at coordinate 0: give it a valid nonzero stride.
+  for (int i = 0; i + 1 < rank; ++i) gstr[i] = (cuuint64_t)(dims[i + 1] == 1 ? 8 : strides[i]) * 2;
+  const CUtensorMapDataType dt = t.dtype == M3_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(map, dt, (cuuint32_t)rank, t.data, gdim, gstr, bdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 template <typename T, int R>
 static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
   // 16-byte vector stores of y need unit element stride and aligned row starts.
@@ -1152,11 +1265,40 @@ static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
     cudaError_t pe = cudaGetLastError();
     if (pe != cudaSuccess) return pe;
   }
+  constexpr uint32_t TOK = Layout<R>::TOK;
+  TileMaps tm;
+  memset(&tm, 0, sizeof(tm));
+  if (!a.reverse) {
+    const uint64_t dq[5] = {(uint64_t)a.d_state, (uint64_t)R, (uint64_t)a.groups, (uint64_t)a.length,
+                            (uint64_t)a.batch};
+    const uint32_t bq[5] = {64, (uint32_t)R, 1, TOK, 1};
+    const int64_t sq[4] = {a.q.stride[3], a.q.stride[2], a.q.stride[1], a.q.stride[0]};
+    const int64_t sk[4] = {a.k.stride[3], a.k.stride[2], a.k.stride[1], a.k.stride[0]};
+    const uint64_t dx[4] = {(uint64_t)a.head_dim, (uint64_t)a.heads, (uint64_t)a.length, (uint64_t)a.batch};
+    const uint32_t bx[4] = {64, 1, TOK, 1};
+    const int64_t sx[3] = {a.value.stride[2], a.value.stride[1], a.value.stride[0]};
+    const int64_t sz[3] = {a.gate.stride[2], a.gate.stride[1], a.gate.stride[0]};
+    if (!encode_rows(&tm.q, a.q, 5, dq, sq, bq) || !encode_rows(&tm.k, a.k, 5, dq, sk, bq) ||
+        !encode_rows(&tm.x, a.value, 4, dx, sx, bx) || !encode_rows(&tm.z, a.gate, 4, dx, sz, bx))
+      return cudaErrorInvalidValue;
+    if (a.workspace.data) {
+      PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+      const int W = ws_stride(R, a.num_angles);
+      const cuuint64_t gdim[3] = {(cuuint64_t)W, (cuuint64_t)a.length, (cuuint64_t)a.batch};
+      const cuuint64_t gstr[2] = {(cuuint64_t)W * 4, (cuuint64_t)a.length * W * 4};
+      const cuuint32_t bdim[3] = {(cuuint32_t)W, TOK, 1}, estr[3] = {1, 1, 1};
+      if (enc == nullptr ||
+          enc(&tm.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.workspace.data, gdim, gstr, bdim, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    }
+  }
   auto kern = scan_umma_kernel<T, R>;
   constexpr uint32_t smem = Layout<R>::SmemBytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(a.heads, a.batch), kThreads, smem, stream>>>(a, vec_y);
+  kern<<<dim3(a.heads, a.batch), kThreads, smem, stream>>>(a, tm, vec_y);
   return cudaGetLastError();
 }
 
@@ -1183,7 +1325,17 @@ int64_t scan_umma_workspace_bytes(const m3_scan_args& a) {
 static bool rows16(const m3_tensor& t, int nd) {
   if ((reinterpret_cast<uintptr_t>(t.data) & 15u) != 0 || t.stride[nd - 1] != 1) return false;
   for (int i = 0; i < nd - 1; ++i)
-    if (t.stride[i] % 8 != 0) return false;
+    if (t.stride[i] % 8 != 0 || t.stride[i] < 0) return false;
+  return true;
+}
+
+// Tensor-map strides: every dimension of extent > 1 advances through memory.
+static bool strided(const m3_tensor& t, std::initializer_list<int64_t> extents) {
+  int i = 0;
+  for (int64_t e : extents) {
+    if (e > 1 && t.stride[i] == 0) return false;
+    ++i;
+  }
   return true;
 }
 
@@ -1191,6 +1343,8 @@ bool scan_umma_supported(const m3_scan_args& a) {
   const bool has_phase = a.phase.data != nullptr || a.angles.data != nullptr;
   return (a.value.dtype == M3_BF16 || a.value.dtype == M3_F16) && a.d_state == umma::kN &&
          rows16(a.q, 5) && rows16(a.k, 5) && rows16(a.value, 4) && rows16(a.gate, 4) &&
+         strided(a.q, {a.batch, a.length, a.groups, a.rank}) && strided(a.k, {a.batch, a.length, a.groups, a.rank}) &&
+         strided(a.value, {a.batch, a.length, a.heads}) && strided(a.gate, {a.batch, a.length, a.heads}) &&
          !(a.q_norm_w.data != nullptr && a.phase.data != nullptr) &&
          a.head_dim == umma::kP && (a.rank == 1 || a.rank == 2 || a.rank == 4 || a.rank == 8) &&
          (!has_phase || (a.mimo_rotation ? a.num_angles == umma::kMaxAngles : a.num_angles <= umma::kMaxAngles));
