@@ -59,13 +59,12 @@ namespace umma {
 // Optional per-section cycle counters of CTA (0, 0), thread 0 (probe builds only).
 #ifdef M3_SECTION_TIMING
 __device__ unsigned long long g_section_cycles[16];
-#define M3_MARK(k)                                                                    \
-  do {                                                                                \
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {                     \
-      const long long now_ = clock64();                                               \
-      g_section_cycles[k] += (unsigned long long)(now_ - mark_prev_);                 \
-      mark_prev_ = now_;                                                              \
-    }                                                                                 \
+// cycles accumulate in registers and are added to g_section_cycles once, at the end
+#define M3_MARK(k)                                            \
+  do {                                                        \
+    const long long now_ = clock64();                         \
+    mark_acc_[k] += (unsigned int)(now_ - mark_prev_);        \
+    mark_prev_ = now_;                                        \
   } while (0)
 #else
 #define M3_MARK(k) \
@@ -104,7 +103,8 @@ template <int R> struct Layout {
   // CBq/CBk: packed bias words [R][64]; CMx/CMz/CMo: MIMO projections (float); CMxp: CMx packed [R][32]
   static constexpr int CBq = kSEnd, CBk = CBq + R * kN, CMx = CBk + R * kN, CMz = CMx + R * kP, CMo = CMz + R * kP;
   static constexpr int CMxp = CMo + R * kP;
-  static constexpr int Ws = ((CMxp + R * kP / 2 + 31) / 32) * 32;  // tile's workspace rows [TOK][WSP] (128 B)
+  static constexpr int CWq = CMxp + R * kP / 2, CWk = CWq + kN / 2;   // packed norm weights [64]
+  static constexpr int Ws = ((CWk + kN / 2 + 31) / 32) * 32;  // tile's workspace rows [TOK][WSP] (128 B)
   static constexpr int Seg = Ws + TOK * WSP;            // [kWarps][32] sums, then [kWarps][32] offsets
   static constexpr int Carry = Seg + 2 * kWarps * 32;   // [0..31] block offset, [32..63] within-block sum
   static constexpr int FEnd = Carry + 64;
@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (use_tma) {
       if (tid == 0) {
         mbar_expect_tx(tma_bar, (uint32_t)(TOK * kP * 2));
-        tma_load4(sbase + kOffW, &tm.x, 0, h, t0n, b, tma_bar);
+        tma_load4(sbase + (R == 1 ? kOffV : kOffW), &tm.x, 0, h, t0n, b, tma_bar);
       }
       return;
     }
@@ -484,7 +484,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int j = c >> 3, c8 = c & 7;
       if (j < ntn) {
         const int t = scan_token(a, t0n + j);
-        cp_async16(sbase + kOffW + swz(j, c8 * 8, kRows), vp + v_b0 + (int64_t)t * a.value.stride[1] + c8 * 8);
+        cp_async16(sbase + (R == 1 ? kOffV : kOffW) + swz(j, c8 * 8, kRows),
+                   vp + v_b0 + (int64_t)t * a.value.stride[1] + c8 * 8);
       }
     }
   };
@@ -594,6 +595,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   uint32_t* cbq = reinterpret_cast<uint32_t*>(cst + Lay::CBq);  // packed bias words [R][64]
   uint32_t* cbk = reinterpret_cast<uint32_t*>(cst + Lay::CBk);
+  uint32_t* cwq = reinterpret_cast<uint32_t*>(cst + Lay::CWq);  // packed norm weights [64]
+  uint32_t* cwk = reinterpret_cast<uint32_t*>(cst + Lay::CWk);
+  for (int i = tid; i < kN / 2; i += kThreads) {
+    const bool nw = a.q_norm_w.data != nullptr;
+    cwq[i] = nw ? pack2<T>(ld_t(a.q_norm_w, 2 * i * a.q_norm_w.stride[0]), ld_t(a.q_norm_w, (2 * i + 1) * a.q_norm_w.stride[0]))
+                : 0u;
+    cwk[i] = nw ? pack2<T>(ld_t(a.k_norm_w, 2 * i * a.k_norm_w.stride[0]), ld_t(a.k_norm_w, (2 * i + 1) * a.k_norm_w.stride[0]))
+                : 0u;
+  }
   for (int i = tid; i < R * kN / 2; i += kThreads) {
     const int r = i / (kN / 2), n = 2 * (i % (kN / 2));
     float bq[2] = {0.0f, 0.0f}, bk[2] = {0.0f, 0.0f};
@@ -623,20 +633,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                          ld_t(mx, h * mx.stride[0] + r * mx.stride[1] + (p + 1) * mx.stride[2]));
     }
   }
-  // Staging: thread (warp, lane) owns the 16-byte chunk cq = lane & 15 (elements 8 cq .. 8 cq + 7)
-  // of rows warp * 8 + 2 i + (lane >> 4). Its norm weights, packed.
-  const int cq = lane & 15;
   const bool has_norm = a.q_norm_w.data != nullptr;
   const bool has_bias = a.q_bias.data != nullptr;
-  uint32_t wq2[4], wk2[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int n = 8 * cq + 2 * e;
-    wq2[e] = has_norm ? pack2<T>(ld_t(a.q_norm_w, n * a.q_norm_w.stride[0]),
-                                 ld_t(a.q_norm_w, (n + 1) * a.q_norm_w.stride[0])) : 0u;
-    wk2[e] = has_norm ? pack2<T>(ld_t(a.k_norm_w, n * a.k_norm_w.stride[0]),
-                                 ld_t(a.k_norm_w, (n + 1) * a.k_norm_w.stride[0])) : 0u;
-  }
   // Loads of the first tile.
   {
     const int nt0 = min(TOK, L);
@@ -698,6 +696,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   float phi = 1.0f;  // TMEM holds S / phi
 #ifdef M3_SECTION_TIMING
   long long mark_prev_ = clock64();
+  unsigned int mark_acc_[16];
+  for (int k_ = 0; k_ < 16; ++k_) mark_acc_[k_] = 0;
 #endif
 
   // Phase carry of this warp's angles 4 warp .. 4 warp + 3 (block offset, in-block sum).
@@ -875,73 +875,82 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool fact = mode[2] != 0.0f;
     M3_MARK(3);
 
-    // ---- stage Q', K' in place (packed 16-bit math): q' = rot(q rq w + b) fq, k' = rot(k rk w + b) fk ----
+    // ---- stage Q', K' in place (packed 16-bit math): q' = rot(q rq w + b) fq, k' = rot(k rk w + b) fk.
+    // Lane: row warp * 8 + 4 it + (lane >> 3), 16-byte chunks c = lane & 7 and c + 8 (elements 8 c ..,
+    // 64 + 8 c ..), so the rotated chunks (the first S pairs; MIMO: n < 32 with n + 64) spread over all
+    // lanes and a MIMO pair never leaves its lane. ----
+    const uint32_t qko = kOffQ;
+    const int c = lane & 7;
 #pragma unroll
-    for (int it = 0; it < kRowsPerWarp / 2; ++it) {
-      const int row = warp * kRowsPerWarp + 2 * it + (lane >> 4);
-      const int j = row / R, r = row % R;
+    for (int it = 0; it < 2; ++it) {
+      const int row = warp * 8 + 4 * it + (lane >> 3);
+      const int ts_ = row / R, r = row % R;
+      const int j = ts_;
       const bool valid = j < nt;
-      const int jc = min(j, TOK - 1);
-      const float* wrow = wsb + jc * WS;
-      const uint32_t off = swz(row, 8 * cq, kRows);
-      const uint4 qraw = *reinterpret_cast<const uint4*>(smem + kOffQ + off);
-      const uint4 kraw = *reinterpret_cast<const uint4*>(smem + kOffK + off);
-      uint32_t qv[4] = {qraw.x, qraw.y, qraw.z, qraw.w};
-      uint32_t kv[4] = {kraw.x, kraw.y, kraw.z, kraw.w};
-      if (has_norm) {
-        const uint32_t rq2 = bcast2<T>(wrow[r]), rk2 = bcast2<T>(wrow[R + r]);
-        const uint4 bq = *reinterpret_cast<const uint4*>(cbq + r * (kN / 2) + 4 * cq);
-        const uint4 bk = *reinterpret_cast<const uint4*>(cbk + r * (kN / 2) + 4 * cq);
-        const uint32_t bqa[4] = {bq.x, bq.y, bq.z, bq.w}, bka[4] = {bk.x, bk.y, bk.z, bk.w};
+      const float* wrow = wsb + ts_ * WS;
+      const uint32_t off0 = qko + swz(row, 8 * c, kRows), off1 = qko + swz(row, 64 + 8 * c, kRows);
+      uint32_t qv[8], kv[8];
+      {
+        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + off0);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(smem + off1);
+        const uint4 k0 = *reinterpret_cast<const uint4*>(smem + off0 + kRows * kN * 2);
+        const uint4 k1 = *reinterpret_cast<const uint4*>(smem + off1 + kRows * kN * 2);
+        qv[0] = q0.x; qv[1] = q0.y; qv[2] = q0.z; qv[3] = q0.w;
+        qv[4] = q1.x; qv[5] = q1.y; qv[6] = q1.z; qv[7] = q1.w;
+        kv[0] = k0.x; kv[1] = k0.y; kv[2] = k0.z; kv[3] = k0.w;
+        kv[4] = k1.x; kv[5] = k1.y; kv[6] = k1.z; kv[7] = k1.w;
+      }
+      if (has_norm || has_bias) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          qv[e] = fma2<T>(mul2<T>(qv[e], rq2), wq2[e], bqa[e]);
-          kv[e] = fma2<T>(mul2<T>(kv[e], rk2), wk2[e], bka[e]);
-        }
-      } else if (has_bias) {
-        const uint4 bq = *reinterpret_cast<const uint4*>(cbq + r * (kN / 2) + 4 * cq);
-        const uint4 bk = *reinterpret_cast<const uint4*>(cbk + r * (kN / 2) + 4 * cq);
-        const uint32_t bqa[4] = {bq.x, bq.y, bq.z, bq.w}, bka[4] = {bk.x, bk.y, bk.z, bk.w};
+        for (int hf = 0; hf < 2; ++hf) {
+          const int wo = 4 * c + 32 * hf;  // first packed word of this chunk
+          const uint4 bq = *reinterpret_cast<const uint4*>(cbq + r * (kN / 2) + wo);
+          const uint4 bk = *reinterpret_cast<const uint4*>(cbk + r * (kN / 2) + wo);
+          const uint32_t bqa[4] = {bq.x, bq.y, bq.z, bq.w}, bka[4] = {bk.x, bk.y, bk.z, bk.w};
+          if (has_norm) {
+            const uint32_t rq2 = bcast2<T>(wrow[r]), rk2 = bcast2<T>(wrow[R + r]);
+            const uint4 wq = *reinterpret_cast<const uint4*>(cwq + wo);
+            const uint4 wk = *reinterpret_cast<const uint4*>(cwk + wo);
+            const uint32_t wqa[4] = {wq.x, wq.y, wq.z, wq.w}, wka[4] = {wk.x, wk.y, wk.z, wk.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          qv[e] = add2<T>(qv[e], bqa[e]);
-          kv[e] = add2<T>(kv[e], bka[e]);
+            for (int e = 0; e < 4; ++e) {
+              qv[4 * hf + e] = fma2<T>(mul2<T>(qv[4 * hf + e], rq2), wqa[e], bqa[e]);
+              kv[4 * hf + e] = fma2<T>(mul2<T>(kv[4 * hf + e], rk2), wka[e], bka[e]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              qv[4 * hf + e] = add2<T>(qv[4 * hf + e], bqa[e]);
+              kv[4 * hf + e] = add2<T>(kv[4 * hf + e], bka[e]);
+            }
+          }
         }
       }
       if (has_phase) {
         const uint32_t* rw = reinterpret_cast<const uint32_t*>(wrow + WA);
         if (a.mimo_rotation) {
-          // pairs (n, n + 64) for n < 32: the partner chunk is cq ^ 8, i.e. lane ^ 8.
-          uint32_t qo[4], ko[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            qo[e] = __shfl_xor_sync(0xffffffffu, qv[e], 8);
-            ko[e] = __shfl_xor_sync(0xffffffffu, kv[e], 8);
-          }
-          if ((cq & 7) < 4) {
-            const int q4 = 4 * (cq & 3);  // first cos/sin word of this chunk's angles
-            const uint4 c4 = *reinterpret_cast<const uint4*>(rw + q4);
-            const uint4 s4 = *reinterpret_cast<const uint4*>(rw + 16 + q4);
+          // pairs (n, n + 64) for n < 32: chunk c < 4 and chunk c + 8 of the same lane
+          if (c < 4) {
+            const uint4 c4 = *reinterpret_cast<const uint4*>(rw + 4 * c);
+            const uint4 s4 = *reinterpret_cast<const uint4*>(rw + 16 + 4 * c);
             const uint32_t ca[4] = {c4.x, c4.y, c4.z, c4.w}, sa[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              if (cq < 8) {  // first half: a c - b s
-                const uint32_t ns = sa[e] ^ 0x80008000u;
-                qv[e] = fma2<T>(qo[e], ns, mul2<T>(qv[e], ca[e]));
-                kv[e] = fma2<T>(ko[e], ns, mul2<T>(kv[e], ca[e]));
-              } else {       // second half: a s + b c
-                qv[e] = fma2<T>(qo[e], sa[e], mul2<T>(qv[e], ca[e]));
-                kv[e] = fma2<T>(ko[e], sa[e], mul2<T>(kv[e], ca[e]));
-              }
+              const uint32_t ns = sa[e] ^ 0x80008000u;
+              const uint32_t qa_ = qv[e], qb_ = qv[4 + e], ka_ = kv[e], kb_ = kv[4 + e];
+              qv[e] = fma2<T>(qb_, ns, mul2<T>(qa_, ca[e]));         // a c - b s
+              qv[4 + e] = fma2<T>(qa_, sa[e], mul2<T>(qb_, ca[e]));  // a s + b c
+              kv[e] = fma2<T>(kb_, ns, mul2<T>(ka_, ca[e]));
+              kv[4 + e] = fma2<T>(ka_, sa[e], mul2<T>(kb_, ca[e]));
             }
           }
-        } else if (4 * cq < S) {
-          // adjacent pairs (2m, 2m + 1), m = 4 cq + e
-          const uint4 c4 = *reinterpret_cast<const uint4*>(rw + 4 * cq);
+        } else if (4 * c < S) {
+          // adjacent pairs (2m, 2m + 1), m = 4 c + e, all in the first chunk
+          const uint4 c4 = *reinterpret_cast<const uint4*>(rw + 4 * c);
           const uint32_t csa[4] = {c4.x, c4.y, c4.z, c4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            if (4 * cq + e < S) {
+            if (4 * c + e < S) {
               const uint32_t cc = __byte_perm(csa[e], 0, 0x1010);
               const uint32_t ms = __byte_perm(csa[e], 0, 0x3232) ^ 0x00008000u;
               qv[e] = rot_pair<T>(qv[e], cc, ms);
@@ -954,37 +963,43 @@ __global__ void __launch_bounds__(kThreads, 2)
         const m3_tensor& fkt = a.final_k;
         T* fkp = static_cast<T*>(fkt.data) + b * fkt.stride[0] + h * fkt.stride[1] + r * fkt.stride[2];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int n = 8 * cq + 2 * e;
+        for (int e = 0; e < 8; ++e) {
+          const int n = (e < 4 ? 8 * c : 64 + 8 * c) + 2 * (e & 3);
           fkp[n * fkt.stride[3]] = from_f<T>(lo16<T>(kv[e]));
           fkp[(n + 1) * fkt.stride[3]] = from_f<T>(hi16<T>(kv[e]));
         }
       }
-      // Rows past the end are zeroed by selection: their shared memory holds stale bytes.
-      const uint32_t fq2 = bcast2<T>(fq[jc]), fk2 = bcast2<T>(fk[jc]);
-      uint4 qo4 = make_uint4(0, 0, 0, 0), ko4 = make_uint4(0, 0, 0, 0);
-      if (valid) {
-        qo4 = make_uint4(mul2<T>(qv[0], fq2), mul2<T>(qv[1], fq2), mul2<T>(qv[2], fq2), mul2<T>(qv[3], fq2));
-        ko4 = make_uint4(mul2<T>(kv[0], fk2), mul2<T>(kv[1], fk2), mul2<T>(kv[2], fk2), mul2<T>(kv[3], fk2));
-      }
-      *reinterpret_cast<uint4*>(smem + kOffQ + off) = qo4;
-      *reinterpret_cast<uint4*>(smem + kOffK + off) = ko4;
+      // Rows outside the sequence (zero-filled by the TMA) would still carry the bias: zero them.
+      const uint32_t fq2 = valid ? bcast2<T>(fq[j]) : 0u, fk2 = valid ? bcast2<T>(fk[j]) : 0u;
+      *reinterpret_cast<uint4*>(smem + off0) =
+          make_uint4(mul2<T>(qv[0], fq2), mul2<T>(qv[1], fq2), mul2<T>(qv[2], fq2), mul2<T>(qv[3], fq2));
+      *reinterpret_cast<uint4*>(smem + off1) =
+          make_uint4(mul2<T>(qv[4], fq2), mul2<T>(qv[5], fq2), mul2<T>(qv[6], fq2), mul2<T>(qv[7], fq2));
+      *reinterpret_cast<uint4*>(smem + off0 + kRows * kN * 2) =
+          make_uint4(mul2<T>(kv[0], fk2), mul2<T>(kv[1], fk2), mul2<T>(kv[2], fk2), mul2<T>(kv[3], fk2));
+      *reinterpret_cast<uint4*>(smem + off1 + kRows * kN * 2) =
+          make_uint4(mul2<T>(kv[4], fk2), mul2<T>(kv[5], fk2), mul2<T>(kv[6], fk2), mul2<T>(kv[7], fk2));
     }
-    // ---- V = x mx_r from the raw x rows parked in the W tile; V2 = V e^{cum_last - cum} when the tile
-    // is not factorised. 16-byte chunks: 64 rows x 8 chunks over 256 threads. ----
+    // ---- V = x mx_r: R = 1 keeps the x rows loaded into the V tile (rows past the end zeroed when they
+    // came by row copies), R > 1 expands the x rows parked in the W tile. V2 = V e^{cum_last - cum} when
+    // the tile is not factorised. 16-byte chunks: 64 rows x 8 chunks over 256 threads. ----
 #pragma unroll
     for (int c = tid; c < kRows * (kP / 8); c += kThreads) {
       const int row = c >> 3, ch = c & 7;
       const int j = row / R, r = row % R;
       const int jc = min(j, TOK - 1);
       uint4 v4 = make_uint4(0, 0, 0, 0);
-      if (j < nt) v4 = *reinterpret_cast<const uint4*>(smem + kOffW + swz(j, 8 * ch, kRows));
       if (R > 1) {
+        if (j < nt) v4 = *reinterpret_cast<const uint4*>(smem + kOffW + swz(j, 8 * ch, kRows));
         const uint4 m4 = *reinterpret_cast<const uint4*>(
             reinterpret_cast<const uint32_t*>(cst + Lay::CMxp) + r * (kP / 2) + 4 * ch);
         v4 = make_uint4(mul2<T>(v4.x, m4.x), mul2<T>(v4.y, m4.y), mul2<T>(v4.z, m4.z), mul2<T>(v4.w, m4.w));
+        *reinterpret_cast<uint4*>(smem + kOffV + swz(row, 8 * ch, kRows)) = v4;
+      } else if (j < nt) {
+        if (!fact) v4 = *reinterpret_cast<const uint4*>(smem + kOffV + swz(row, 8 * ch, kRows));
+      } else if (!use_tma) {
+        *reinterpret_cast<uint4*>(smem + kOffV + swz(row, 8 * ch, kRows)) = v4;
       }
-      *reinterpret_cast<uint4*>(smem + kOffV + swz(row, 8 * ch, kRows)) = v4;
       if (!fact) {
         const uint32_t e2 = bcast2<T>(edec[jc]);
         *reinterpret_cast<uint4*>(smem + kOffV2 + swz(row, 8 * ch, kRows)) =
@@ -1196,6 +1211,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (*abort_flag) break;
   }
   cp_async_wait_all();
+#ifdef M3_SECTION_TIMING
+  if (blockIdx.x == 0 && blockIdx.y == 0 && tid == 0)
+    for (int k_ = 0; k_ < 16; ++k_) atomicAdd(&g_section_cycles[k_], (unsigned long long)mark_acc_[k_]);
+#endif
 
   // ---- final state: S[p][n] = phi X^T ----
   fence_after();
