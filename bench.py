@@ -229,8 +229,9 @@ def run_prefill(args, world, rank, local):
     flops_launch = scan_flops_per_token_layer(model, 128 // mrank if mrank > 1 else 128) * batch * length
     achieved = bytes_launch / (kernel_ms / 1e3) / 1e9
     tflops = flops_launch / (kernel_ms / 1e3) / 1e12
-    # per layer and direction: the token pre-pass and the chunked-SSD kernel
-    launches_per_step = depth * 2 * (1 if causal else 2)
+    # per layer and direction: the token pre-pass and the chunked-SSD kernel; per block boundary one
+    # fused residual add + RMSNorm
+    launches_per_step = depth * 2 * (1 if causal else 2) + depth + 1  # + residual add / RMSNorm kernels
     result = {
         "metric": "prefill_tokens_per_s",
         "value": value,

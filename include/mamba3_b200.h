@@ -135,6 +135,25 @@ typedef struct m3_step_args {
   m3_tensor q_norm_w, k_norm_w, dt_bias;
 } m3_step_args;
 
+/*
+ * Residual add + RMSNorm between blocks, one pass (mamba3/model.py:487-520 block
+ * `hidden + mixer(norm(hidden))` with norm = F.rms_norm(x, w.to(x.dtype), eps), and the cast of
+ * the normalised rows to the next in_proj's input dtype under autocast):
+ *   r = x (+ m);  out_x = r (optional, may alias x);  out_n = round(r * rsqrt(mean(r^2) + eps) * w)
+ *   x, m, out_x, out_n  [rows, dim] (element strides);  w [dim];  out_n may not alias x or m.
+ * The reference does this with separate PyTorch ops (add, rms_norm, dtype cast); no Triton kernel
+ * of the reference corresponds to it.
+ */
+typedef struct m3_norm_args {
+  int64_t rows;
+  int32_t dim, device;  /* device: CUDA ordinal of the tensors and `stream` (-1: current) */
+  float eps;
+  int32_t reserved;
+  m3_tensor x, m, w, out_x, out_n;
+} m3_norm_args;
+
+int m3_residual_rmsnorm(const m3_norm_args* args, void* stream);
+
 /* Chunked SSD forward. Returns M3_OK or an M3_ERR_* code. */
 int m3_scan_fwd(const m3_scan_args* args, void* stream);
 

@@ -58,6 +58,12 @@ class ScanArgs(ctypes.Structure):
         (name, M3Tensor) for name in _SCAN_TENSORS]
 
 
+class NormArgs(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_int64), ("dim", ctypes.c_int32), ("device", ctypes.c_int32),
+                ("eps", ctypes.c_float), ("reserved", ctypes.c_int32)] + [
+        (name, M3Tensor) for name in ("x", "m", "w", "out_x", "out_n")]
+
+
 class StepArgs(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in (
         "batch", "heads", "rank", "d_state", "head_dim", "num_angles", "device")] + [
@@ -99,6 +105,8 @@ def load() -> ctypes.CDLL:
         lib.m3_scan_workspace_bytes.restype = ctypes.c_int64
         lib.m3_step_workspace_bytes.argtypes = [ctypes.POINTER(StepArgs)]
         lib.m3_step_workspace_bytes.restype = ctypes.c_int64
+        lib.m3_residual_rmsnorm.argtypes = [ctypes.POINTER(NormArgs), ctypes.c_void_p]
+        lib.m3_residual_rmsnorm.restype = ctypes.c_int
         lib.m3_last_scan_kernel.argtypes = []
         lib.m3_last_scan_kernel.restype = ctypes.c_char_p
         if lib.m3_abi_version() != ABI_VERSION:
@@ -187,6 +195,26 @@ def step_forward(*, sizes: dict, tensors: dict, norm_eps: float = 1e-5) -> None:
         args.workspace = _desc(workspace)
     stream = torch.cuda.current_stream(device).cuda_stream
     _check(lib.m3_step_fwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
+
+
+@torch.compiler.disable
+def residual_rmsnorm(x: torch.Tensor, m: torch.Tensor | None, w: torch.Tensor, eps: float, *,
+                     out_dtype: torch.dtype, out_x: torch.Tensor | None = None) -> torch.Tensor:
+    """Enqueue ``m3_residual_rmsnorm`` over the rows of x (+ m): writes the updated residual into
+    ``out_x`` when given and returns the normalised rows in ``out_dtype``."""
+    lib = load()
+    d = x.shape[-1]
+    x2 = x.reshape(-1, d)
+    out_n = torch.empty(x2.shape, device=x.device, dtype=out_dtype)
+    args = NormArgs()
+    args.rows, args.dim, args.eps = x2.shape[0], d, float(eps)
+    args.device = x.device.index if x.device.index is not None else torch.cuda.current_device()
+    args.x, args.w, args.out_n = _desc(x2), _desc(w), _desc(out_n)
+    args.m = _desc(m.reshape(-1, d) if m is not None else None)
+    args.out_x = _desc(out_x.reshape(-1, d) if out_x is not None else None)
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    _check(lib.m3_residual_rmsnorm(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
+    return out_n.view(x.shape)
 
 
 def last_scan_kernel() -> str:

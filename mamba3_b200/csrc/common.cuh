@@ -52,6 +52,13 @@ __device__ __forceinline__ float ld_any(const void* p, int dtype, int64_t idx) {
 
 __device__ __forceinline__ float ld_t(const m3_tensor& t, int64_t idx) { return ld_any(t.data, t.dtype, idx); }
 
+// Store `v` (rounded to nearest) as element `idx` of a tensor whose dtype is known at run time.
+__device__ __forceinline__ void st_t(const m3_tensor& t, int64_t idx, float v) {
+  if (t.dtype == M3_F32) static_cast<float*>(t.data)[idx] = v;
+  else if (t.dtype == M3_BF16) static_cast<__nv_bfloat16*>(t.data)[idx] = __float2bfloat16_rn(v);
+  else static_cast<__half*>(t.data)[idx] = __float2half_rn(v);
+}
+
 // ---------------------------------------------------------------------------
 // Scalar maps (mamba3/model.py:195-198, mamba3/ops.py:28-32)
 // ---------------------------------------------------------------------------

@@ -391,9 +391,39 @@ class Mamba3(nn.Module):
         self._validate_input(x)
         if x.shape[0] == 0 or x.shape[1] == 0:
             return self._empty_output(x)
+        if self._fused_stream(x):
+            return self._forward_fused(x, want_cache=False)
         for layer in self.layers:
             x = layer(x)
         return self.norm_f(x)
+
+    def _fused_stream(self, x: torch.Tensor) -> bool:
+        """CUDA inference: the residual stream between blocks runs through one fused kernel."""
+        return x.is_cuda and _kernel_eligible(x, *self.parameters())
+
+    def _forward_fused(self, x: torch.Tensor, *, want_cache: bool):
+        """Blocks as norm -> mixer -> (residual add + next norm) in one pass (m3_residual_rmsnorm):
+        the same arithmetic as `hidden + mixer(norm(hidden))` per block and `norm_f` at the end, with
+        each normalised row written once in the dtype the next in_proj reads."""
+        act = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
+        first = self.layers[0].norm
+        normed = _ext.residual_rmsnorm(x, None, first.weight, first.eps, out_dtype=act)
+        resid, caches = x, []
+        for i, layer in enumerate(self.layers):
+            if want_cache:
+                mixed, layer_cache = layer.mixer(normed, return_cache=True)
+                caches.append(layer_cache)
+            else:
+                mixed = layer.mixer(normed)
+            if i + 1 == len(self.layers):
+                out = _ext.residual_rmsnorm(resid, mixed, self.norm_f.weight, self.norm_f.eps, out_dtype=x.dtype)
+                return (out, caches) if want_cache else out
+            nxt = self.layers[i + 1].norm
+            if resid is x:  # never write into the caller's input
+                resid = torch.empty_like(x)
+                normed = _ext.residual_rmsnorm(x, mixed, nxt.weight, nxt.eps, out_dtype=act, out_x=resid)
+            else:
+                normed = _ext.residual_rmsnorm(resid, mixed, nxt.weight, nxt.eps, out_dtype=act, out_x=resid)
 
     def prefill(self, x: torch.Tensor):
         """Process a causal prefix and return the constant-size decode cache."""
@@ -402,6 +432,8 @@ class Mamba3(nn.Module):
         self._validate_input(x)
         if x.shape[0] == 0 or x.shape[1] == 0:
             raise ValueError("prefill requires a non-empty batch and sequence")
+        if self._fused_stream(x):
+            return self._forward_fused(x, want_cache=True)
         caches = []
         for layer in self.layers:
             x, layer_cache = layer(x, return_cache=True)

@@ -38,6 +38,18 @@ def test_struct_layout_matches_header():
     assert ctypes.sizeof(_ext.M3Tensor) == 64
     assert ctypes.sizeof(_ext.ScanArgs) == 14 * 4 + 27 * 64
     assert ctypes.sizeof(_ext.StepArgs) == 8 * 4 + 26 * 64
+    assert ctypes.sizeof(_ext.NormArgs) == 8 + 4 * 4 + 5 * 64
+
+
+def test_residual_rmsnorm_rejects_bad_arguments_without_a_device():
+    lib = _ext.load()
+    assert lib.m3_residual_rmsnorm(None, None) == 4
+    args = _ext.NormArgs()
+    args.rows, args.dim, args.device = 4, 128, -1
+    assert lib.m3_residual_rmsnorm(ctypes.byref(args), None) == 4  # x / w / out_n missing
+    assert b"required" in lib.m3_last_error()
+    args.dim = 0
+    assert lib.m3_residual_rmsnorm(ctypes.byref(args), None) == 1
 
 
 def test_null_and_invalid_arguments_are_rejected_without_a_device():

@@ -88,6 +88,62 @@ def test_low_precision_model_kernels_vs_pytorch(rank, dtype):
     torch.testing.assert_close(cont, expected, rtol=3e-2, atol=3e-2)
 
 
+def _layer_by_layer(model, x, want_cache=False):
+    """The block loop of the reference (`hidden + mixer(norm(hidden))`, then norm_f), op by op."""
+    caches = []
+    for layer in model.layers:
+        if want_cache:
+            x, c = layer(x, return_cache=True)
+            caches.append(c)
+        else:
+            x = layer(x)
+    return (model.norm_f(x), caches) if want_cache else model.norm_f(x)
+
+
+@pytest.mark.parametrize("autocast", [False, True])
+def test_fused_residual_stream_matches_block_loop(autocast):
+    """Mamba3.forward / prefill on CUDA run the residual add and the next RMSNorm as one kernel
+    (m3_residual_rmsnorm); the result must equal the reference block loop."""
+    torch.manual_seed(3)
+    model = Mamba3(256, d_state=128, depth=3).cuda().eval()
+    for layer in model.layers:  # non-trivial norm weights
+        layer.norm.weight.data.uniform_(0.5, 1.5)
+    model.norm_f.weight.data.uniform_(0.5, 1.5)
+    x = torch.randn(2, 200, 256, device="cuda")
+    x_copy = x.clone()
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+        fused = model(x)
+        expected = _layer_by_layer(model, x)
+        out_p, caches = model.prefill(x)
+        exp_p, exp_caches = _layer_by_layer(model, x, want_cache=True)
+    tol = 2e-2 if autocast else 1e-5
+    assert fused.dtype == expected.dtype == torch.float32
+    assert rel_err(fused, expected) < tol
+    assert rel_err(out_p, exp_p) < tol
+    for got, want in zip(caches, exp_caches):
+        assert rel_err(got[1], want[1]) < (1e-2 if autocast else 1e-5)
+    torch.testing.assert_close(x, x_copy, rtol=0, atol=0)  # the input is not written
+
+
+def test_residual_rmsnorm_kernel_against_torch():
+    torch.manual_seed(4)
+    x = torch.randn(37, 1024, device="cuda")
+    m = torch.randn(37, 1024, device="cuda", dtype=torch.bfloat16)
+    w = torch.rand(1024, device="cuda") + 0.5
+    out_x = torch.empty_like(x)
+    n = _ext.residual_rmsnorm(x, m, w, 1e-5, out_dtype=torch.bfloat16, out_x=out_x)
+    r = x + m.float()
+    torch.testing.assert_close(out_x, r, rtol=0, atol=0)
+    ref = torch.nn.functional.rms_norm(r, (1024,), w, 1e-5)
+    torch.testing.assert_close(n.float(), ref, rtol=1e-2, atol=1e-2)
+    # generic path: odd width, strided rows, fp32 output, in place residual
+    x2 = torch.randn(5, 300, device="cuda")[:, :200]
+    expect = torch.nn.functional.rms_norm(x2 + 1.0, (200,), w[:200], 1e-5)
+    n2 = _ext.residual_rmsnorm(x2, torch.ones(5, 200, device="cuda"), w[:200], 1e-5, out_dtype=torch.float32,
+                               out_x=x2)
+    torch.testing.assert_close(n2, expect, rtol=1e-5, atol=1e-5)
+
+
 def test_cuda_graph_decoder_matches_forward_and_resets():
     torch.manual_seed(5)
     model = Mamba3(64, d_state=128, depth=1).cuda().eval()
