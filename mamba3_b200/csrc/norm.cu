@@ -54,6 +54,43 @@ __global__ void __launch_bounds__(kNormThreads) residual_rmsnorm_kernel(const m3
   }
 }
 
+// Few rows (a decode step: one row per sequence): one CTA of kNormThreads per row, any dtypes.
+__global__ void __launch_bounds__(kNormThreads) residual_rmsnorm_rowblock(const m3_norm_args a) {
+  __shared__ float part[kNormThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int D = a.dim, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t xo = row * a.x.stride[0], mo = row * a.m.stride[0];
+  auto resid = [&](int i) {
+    float r = ld_t(a.x, xo + i * a.x.stride[1]);
+    if (a.m.data) {
+      r += ld_t(a.m, mo + i * a.m.stride[1]);
+      if (a.x.dtype == M3_BF16) r = rnd<__nv_bfloat16>(r);
+      else if (a.x.dtype == M3_F16) r = rnd<__half>(r);
+    }
+    return r;
+  };
+  float ss = 0.0f;
+  for (int i = tid; i < D; i += kNormThreads) {
+    const float r = resid(i);
+    ss += r * r;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) part[warp] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) tot += part[w];
+  const float inv = rsqrtf(tot / D + a.eps);
+  for (int i = tid; i < D; i += kNormThreads) {
+    const float r = resid(i);
+    if (a.out_x.data) st_t(a.out_x, row * a.out_x.stride[0] + i * a.out_x.stride[1], r);
+    float w = ld_t(a.w, i * a.w.stride[0]);
+    if (a.x.dtype == M3_BF16) w = rnd<__nv_bfloat16>(w);
+    else if (a.x.dtype == M3_F16) w = rnd<__half>(w);
+    st_t(a.out_n, row * a.out_n.stride[0] + i * a.out_n.stride[1], r * inv * w);
+  }
+}
+
 // Vector path: fp32 residual, dim % 128 == 0, contiguous 16-byte aligned rows; m and out_n 16-bit
 // (TM / TN) or fp32. Each lane owns float4 groups lane, lane + 32, ... (NV of them, up to 16).
 template <typename TM, typename TN, int NV>
@@ -159,7 +196,10 @@ extern "C" int m3_residual_rmsnorm(const m3_norm_args* args, void* stream) {
                                   (a.m.stride[0] * msz) % (4 * msz) == 0)) &&
                    (!a.out_x.data || rowvec(a.out_x, 4));
   cudaError_t e;
-  if (vec) {
+  if (a.rows < 8 * 148) {  // too few rows for a warp each to fill the GPU
+    residual_rmsnorm_rowblock<<<(unsigned)a.rows, kNormThreads, 0, st>>>(a);
+    e = cudaGetLastError();
+  } else if (vec) {
     switch (a.m.data ? a.m.dtype : M3_BF16) {
       case M3_BF16: e = launch_vec_n<__nv_bfloat16>(a, grid, st); break;
       case M3_F16: e = launch_vec_n<__half>(a, grid, st); break;
