@@ -82,6 +82,8 @@ class _Mamba3Mixer(nn.Module):
         # Set by _CudaGraphDecoder while it captures: the step kernel then writes the state into
         # the cache tensor it was given (the decoder owns that cache).
         self._state_in_place = False
+        # Autocast copies of the projection weights, kept across calls (see _project_linear).
+        self._weight_casts: dict[tuple[str, torch.dtype], tuple[int, int, torch.Tensor]] = {}
 
         width = 2 * self.d_inner + 2 * d_state * self.ngroups * mimo_rank + 3 * self.nheads + self.num_angles
         # Parameter creation order matches the reference so seeded initialisation is identical.
@@ -116,6 +118,23 @@ class _Mamba3Mixer(nn.Module):
         bc = self.d_state * self.ngroups * self.mimo_rank
         return torch.split(projected, (self.d_inner, self.d_inner, bc, bc, self.nheads, self.nheads, self.nheads,
                                        self.num_angles), dim=-1)
+
+    def _project_linear(self, name: str, hidden: torch.Tensor) -> torch.Tensor:
+        """``getattr(self, name)(hidden)`` on the kernel path. Under CUDA autocast the fp32 weight is
+        cast to the autocast dtype once and the copy reused until the weight changes (same storage and
+        version counter), instead of once per autocast region; the product is bit-identical."""
+        layer = getattr(self, name)
+        weight = layer.weight
+        if not (hidden.is_cuda and torch.is_autocast_enabled("cuda") and weight.dtype == torch.float32):
+            return layer(hidden)
+        dtype = torch.get_autocast_dtype("cuda")
+        key = (name, dtype)
+        stamp = (weight.data_ptr(), weight._version)
+        entry = self._weight_casts.get(key)
+        if entry is None or entry[:2] != stamp:
+            entry = (*stamp, weight.detach().to(dtype))
+            self._weight_casts[key] = entry
+        return F.linear(hidden.to(dtype), entry[2])
 
     def _views(self, projected: torch.Tensor):
         batch, length, _ = projected.shape
@@ -213,16 +232,16 @@ class _Mamba3Mixer(nn.Module):
         return self._forward_torch(hidden_states, cache, return_cache)
 
     def _forward_kernels(self, hidden_states, cache, return_cache):
-        projected = self.in_proj(hidden_states)
+        projected = self._project_linear("in_proj", hidden_states)
         mixed, state, phase, k_last, x = self._scan_fused(projected, cache, reverse=False, want_cache=return_cache)
-        output = self.out_proj(mixed.flatten(-2))
+        output = self._project_linear("out_proj", mixed.flatten(-2))
         if self.causal:
             if not return_cache:
                 return output
             return output, (phase, state, k_last, x[:, -1].clone())
         # Backward direction: same projections read back to front, phase restarted at the end.
         mixed_r, _, _, _, _ = self._scan_fused(projected, None, reverse=True, want_cache=False)
-        backward = self.out_proj(mixed_r.flatten(-2))
+        backward = self._project_linear("out_proj", mixed_r.flatten(-2))
         blend = torch.sigmoid(self.direction_logit).to(output.dtype)
         return output * blend + backward * (1.0 - blend)
 
@@ -289,7 +308,7 @@ class _Mamba3Mixer(nn.Module):
             # Model mode: B/C RMS-norm, softplus(delta + dt_bias), the heavy-tail decay, bias and
             # rotation all happen in the kernel, on raw views of the projection (q/k unexpanded,
             # stride 0 over heads).
-            z, x, B, C, delta, decay, trap, angles = self._views(self.in_proj(hidden_states))
+            z, x, B, C, delta, decay, trap, angles = self._views(self._project_linear("in_proj", hidden_states))
             if cache is None:
                 cache = self.allocate_cache(hidden_states.shape[0], device=hidden_states.device, dtype=x.dtype)
             if cache[2].dtype == C.dtype and cache[3].dtype == x.dtype:
@@ -304,7 +323,7 @@ class _Mamba3Mixer(nn.Module):
                     k_bias=self.B_bias, out_state=cache[1] if self._state_in_place else None,
                     q_norm_w=self.C_norm.weight, k_norm_w=self.B_norm.weight, dt_bias=self.dt_bias,
                     norm_eps=self.C_norm.eps)
-                return self.out_proj(mixed.flatten(-2)).unsqueeze(1), next_cache
+                return self._project_linear("out_proj", mixed.flatten(-2)).unsqueeze(1), next_cache
         q, k, x, z, adt, dt, trap, angles = self._project(hidden_states)
         if cache is None:
             cache = self.allocate_cache(hidden_states.shape[0], device=hidden_states.device, dtype=x.dtype)

@@ -232,3 +232,30 @@ def test_negative_phase_increments_do_not_drift_at_long_context():
     expected = torch.remainder(pos * inc, 2 * math.pi).float()[None, :, None, None].expand_as(phase)
     circ = torch.remainder(phase - expected + math.pi, 2 * math.pi) - math.pi
     assert circ.abs().max() < 2e-3
+
+
+def test_autocast_weight_cast_cache_is_exact_and_invalidated():
+    """The kernel path keeps bf16 copies of in_proj/out_proj across autocast regions; the output
+    equals a fresh autocast cast bit for bit and follows in-place weight updates."""
+    torch.manual_seed(8)
+    model = Mamba3(128, d_state=64, depth=2).cuda().eval()
+    x = torch.randn(2, 70, 128, device="cuda")
+
+    def run():
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return model(x)
+
+    def fresh():
+        for layer in model.layers:
+            layer.mixer._weight_casts.clear()
+        return run()
+
+    first = run()
+    torch.testing.assert_close(run(), first, rtol=0, atol=0)
+    torch.testing.assert_close(fresh(), first, rtol=0, atol=0)
+    with torch.no_grad():
+        model.layers[1].mixer.in_proj.weight.mul_(1.5)
+        model.layers[0].mixer.out_proj.weight.add_(0.01)
+    updated = run()
+    assert rel_err(updated, first) > 1e-3
+    torch.testing.assert_close(fresh(), updated, rtol=0, atol=0)
