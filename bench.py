@@ -232,6 +232,18 @@ def run_prefill(args, world, rank, local):
     # per layer and direction: the token pre-pass and the chunked-SSD kernel; per block boundary one
     # fused residual add + RMSNorm
     launches_per_step = depth * 2 * (1 if causal else 2) + depth + 1  # + residual add / RMSNorm kernels
+    traffic = (SCAN_TRAFFIC_PER_TOKEN[args.workload] * batch * length
+               if args.workload in SCAN_TRAFFIC_PER_TOKEN and mrank == 1 and d_model == 1024 else None)
+    common = {"peak_kind": pk_kind, "kernel": f"m3 scan ({kernel_name})", "kernel_ms": kernel_ms,
+              "algorithmic_bytes_per_launch": bytes_launch, "algorithmic_flops_per_launch": flops_launch}
+    if mrank > 1:  # arithmetic intensity above the ridge: graded on the tensor pipe
+        roofline = {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": tflops / pk["bf16_tflops"], "traffic": traffic, **common,
+                    "hbm_gbs": achieved, "hbm_frac": achieved / pk["hbm_gbs"]}
+    else:
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / pk["hbm_gbs"], "traffic": traffic, **common,
+                    "tensor_tflops": tflops, "tensor_frac": tflops / pk["bf16_tflops"]}
     result = {
         "metric": "prefill_tokens_per_s",
         "value": value,
@@ -255,24 +267,19 @@ def run_prefill(args, world, rank, local):
                 "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"],
-                     "traffic": (SCAN_TRAFFIC_PER_TOKEN[args.workload] * batch * length
-                                 if args.workload in SCAN_TRAFFIC_PER_TOKEN and mrank == 1 and d_model == 1024
-                                 else None), "peak_kind": pk_kind,
-                     "kernel": f"m3 scan ({kernel_name})", "kernel_ms": kernel_ms,
-                     "algorithmic_bytes_per_launch": bytes_launch,
-                     "tensor_tflops": tflops, "tensor_frac": tflops / pk["bf16_tflops"]},
+        "roofline": roofline,
     }
     return result
 
 
 def run_decode(args, world, rank):
-    """CUDA-graph decode step of Mamba3(2560, depth=32) at batch 64 (bf16 params, FP32 state)."""
+    """CUDA-graph decode step of Mamba3(2560, depth=32) at batch 64 (bf16 params, FP32 state);
+    `--only decode` with `--batch` / `--depth` / `--decode-rank` measures the other decode cases."""
     from mamba3_b200 import ops
     batch = (args.batch if args.only == "decode" and args.batch else DECODE["batch"])
     depth = (args.depth if args.only == "decode" and args.depth else DECODE["depth"])
-    model = build_model(DECODE["d_model"], depth, 1, True).to(torch.bfloat16)
+    drank = args.decode_rank
+    model = build_model(DECODE["d_model"], depth, drank, True).to(torch.bfloat16)
     decoder = model.cuda_graph(batch_size=batch)
     g = torch.Generator(device="cuda").manual_seed(99 + rank)
     xs = torch.randn(16, batch, 1, DECODE["d_model"], device="cuda", dtype=torch.bfloat16, generator=g)
@@ -291,18 +298,31 @@ def run_decode(args, world, rank):
 
         def kern():
             ops._step_device(qh, kh, xv[:, 0], z[:, 0], adt[:, 0], dt[:, 0], trap[:, 0], ang[:, 0], mixer.D, cache,
-                             mimo_x=None, mimo_z=None, mimo_out=None, q_bias=mixer.C_bias, k_bias=mixer.B_bias,
+                             mimo_x=mixer.mimo_x, mimo_z=mixer.mimo_z, mimo_out=mixer.mimo_out,
+                             q_bias=mixer.C_bias, k_bias=mixer.B_bias,
                              out_state=cache[1])
         for _ in range(3):
             kern()
-        kus = timed(kern, 50, world) * 1e3
+        # Timed as a graph replay, as the decoder runs it: at small batch a Python-launched call
+        # measures the host, not the kernels.
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            kern()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            kern()
+        kus = timed(graph.replay, 50, world) * 1e3
     del mixer_input
     pk, _ = peaks()
     state_bytes = 2 * batch * mixer.nheads * mixer.headdim * mixer.d_state * 4
-    return {"us_per_step": us, "batch": batch, "model": f"Mamba3(2560, depth={depth}, mimo_rank=1) bf16",
+    return {"us_per_step": us, "batch": batch, "model": f"Mamba3(2560, depth={depth}, mimo_rank={drank}) bf16",
             "step_kernel_us": kus, "step_kernel_state_gbs": state_bytes / (kus / 1e6) / 1e9,
             "step_kernel_frac": state_bytes / (kus / 1e6) / 1e9 / pk["hbm_gbs"],
-            "state_bytes_per_layer": state_bytes}
+            "state_bytes_per_layer": state_bytes,
+            # one layer's state below the 126 MB L2 stays cached between replays of the kernel alone
+            "step_kernel_l2_resident": state_bytes < 126e6}
 
 
 def cpu_baseline(args, sample_tokens=None) -> dict:
@@ -341,6 +361,7 @@ def main():
     p.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling cases)")
     p.add_argument("--seq-len", type=int, default=0, help="override the sequence length (profiling cases)")
     p.add_argument("--depth", type=int, default=0, help="override the depth (profiling cases)")
+    p.add_argument("--decode-rank", type=int, default=1, help="MIMO rank of the decode model")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
 
