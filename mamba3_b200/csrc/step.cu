@@ -448,6 +448,183 @@ __global__ void __launch_bounds__(kStepThreads) step_prep_kernel(const m3_step_a
   }
 }
 
+// Unpack eight 16-bit values of a 16-byte word.
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4 w, float* out) {
+  const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = to_f(e[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  uint4 w;
+  T* e = reinterpret_cast<T*>(&w);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) e[i] = from_f<T>(v[i]);
+  return w;
+}
+
+// step_prep_kernel for N = 128 with contiguous, 16-byte aligned 16-bit q / k / out_k rows: the same
+// per-element arithmetic, laid out so that each lane owns whole rotation pairs. Unit u (lane u,
+// u < 8 R) is row u / 8, pairs m = 8 c .. 8 c + 7 with c = u % 8: SISO elements 16 c .. 16 c + 15
+// (pairs (2m, 2m + 1)), MIMO elements 8 c .. 8 c + 7 and 64 + 8 c .. (pairs (m, m + 64)). The RMS
+// sums of a row close within its 8 lanes; all row loads and stores are 16-byte vectors.
+template <typename T, int R>
+__global__ void __launch_bounds__(kStepThreads) step_prep_vec_kernel(const m3_step_args a) {
+  constexpr int N = 128, kUnits = 8 * R;
+  constexpr bool kMimo = R > 1;
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * (kStepThreads / 32) + (threadIdx.x >> 5);
+  if (wid >= (int64_t)a.batch * a.heads) return;
+  const int b = (int)(wid / a.heads), h = (int)(wid % a.heads);
+  const int S = a.num_angles;
+  float* ws = static_cast<float*>(a.workspace.data) + wid * (2 * R * N + 4);
+  const T* qp = static_cast<const T*>(a.q.data);
+  const T* kp = static_cast<const T*>(a.k.data);
+
+  float dtv, adtv;
+  step_dt_adt(a, b, h, dtv, adtv);
+  const float trapv = ld_t(a.trap, b * a.trap.stride[0] + h * a.trap.stride[1]);
+  const float Dh = ld_t(a.D, h * a.D.stride[0]);
+  float th[2] = {0.f, 0.f}, old[2] = {0.f, 0.f};
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int sidx = lane + 32 * u;
+    if (sidx < S) {
+      th[u] = ld_t(a.angle_rate, b * a.angle_rate.stride[0] + sidx * a.angle_rate.stride[1]);
+      old[u] = ld_t(a.phase, b * a.phase.stride[0] + h * a.phase.stride[1] + sidx * a.phase.stride[2]);
+    }
+  }
+  // Raw q / k of this lane's units, issued before the phase arithmetic.
+  constexpr int kIters = (kUnits + 31) / 32;
+  float q[kIters][16], k[kIters][16];
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const int u = lane + 32 * it, r = min(u, kUnits - 1) / 8, c = u % 8;
+    const int64_t qb = b * a.q.stride[0] + h * a.q.stride[1] + r * a.q.stride[2];
+    const int64_t kb = b * a.k.stride[0] + h * a.k.stride[1] + r * a.k.stride[2];
+    const int o0 = kMimo ? 8 * c : 16 * c, o1 = kMimo ? 64 + 8 * c : 16 * c + 8;
+    uint4 w[4] = {};
+    if (u < kUnits) {
+      w[0] = *reinterpret_cast<const uint4*>(qp + qb + o0);
+      w[1] = *reinterpret_cast<const uint4*>(qp + qb + o1);
+      w[2] = *reinterpret_cast<const uint4*>(kp + kb + o0);
+      w[3] = *reinterpret_cast<const uint4*>(kp + kb + o1);
+    }
+    unpack8<T>(w[0], q[it]);
+    unpack8<T>(w[1], q[it] + 8);
+    unpack8<T>(w[2], k[it]);
+    unpack8<T>(w[3], k[it] + 8);
+  }
+  // New phase: lane s owns angles s and s + 32.
+  float cs[2] = {1.f, 1.f}, sn[2] = {0.f, 0.f};
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int sidx = lane + 32 * u;
+    if (sidx < S) {
+      const float inc = fmodf((kPi * tanhf(th[u])) * dtv, kTwoPi);
+      const float ph = fmodf(old[u] + inc, kTwoPi);
+      const m3_tensor& o = a.out_phase;
+      static_cast<float*>(o.data)[b * o.stride[0] + h * o.stride[1] + sidx * o.stride[2]] = ph;
+      float s_, c_;
+      __sincosf(ph, &s_, &c_);  // |ph| < 2 pi: absolute error ~1e-6
+      cs[u] = rnd<T>(c_);
+      sn[u] = rnd<T>(s_);
+    }
+  }
+  const bool has_norm = a.q_norm_w.data != nullptr;
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const int u = lane + 32 * it, r = min(u, kUnits - 1) / 8, c = u % 8;
+    const int o0 = kMimo ? 8 * c : 16 * c, o1 = kMimo ? 64 + 8 * c : 16 * c + 8;
+    if (has_norm) {
+      float sq = 0.f, sk = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        sq += q[it][i] * q[it][i];
+        sk += k[it][i] * k[it][i];
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        sk += __shfl_xor_sync(0xffffffffu, sk, off);
+      }
+      const float rq = rsqrtf(sq / N + a.norm_eps), rk = rsqrtf(sk / N + a.norm_eps);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int e = i < 8 ? o0 + i : o1 + i - 8;
+        q[it][i] = norm_elem<T>(q[it][i], rq, a.q_norm_w, e);
+        k[it][i] = norm_elem<T>(k[it][i], rk, a.k_norm_w, e);
+      }
+    }
+    if (a.q_bias.data) {
+      const m3_tensor& qb_ = a.q_bias;
+      const m3_tensor& kb_ = a.k_bias;
+      const int64_t qo = h * qb_.stride[0] + r * qb_.stride[1];
+      const int64_t ko = h * kb_.stride[0] + r * kb_.stride[1];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int e = i < 8 ? o0 + i : o1 + i - 8;
+        q[it][i] = rnd<T>(q[it][i] + rnd<T>(ld_t(qb_, qo + e * qb_.stride[2])));
+        k[it][i] = rnd<T>(k[it][i] + rnd<T>(ld_t(kb_, ko + e * kb_.stride[2])));
+      }
+    }
+    // Rotation of pairs m = 8 c + j < S; (cos, sin) of angle m come from lane m % 32.
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int m = 8 * c + j;
+      float cv = __shfl_sync(0xffffffffu, cs[0], m & 31), sv = __shfl_sync(0xffffffffu, sn[0], m & 31);
+      if (S > 32) {  // warp-uniform
+        const float c1 = __shfl_sync(0xffffffffu, cs[1], m & 31), s1 = __shfl_sync(0xffffffffu, sn[1], m & 31);
+        if (m >= 32) {
+          cv = c1;
+          sv = s1;
+        }
+      }
+      if (m < S) {
+        const int i0 = kMimo ? j : 2 * j, i1 = kMimo ? j + 8 : 2 * j + 1;
+        const float a0 = q[it][i0], a1 = q[it][i1], b0 = k[it][i0], b1 = k[it][i1];
+        q[it][i0] = rnd<T>(rnd<T>(a0 * cv) - rnd<T>(a1 * sv));
+        q[it][i1] = rnd<T>(rnd<T>(a0 * sv) + rnd<T>(a1 * cv));
+        k[it][i0] = rnd<T>(rnd<T>(b0 * cv) - rnd<T>(b1 * sv));
+        k[it][i1] = rnd<T>(rnd<T>(b0 * sv) + rnd<T>(b1 * cv));
+      }
+    }
+    if (u < kUnits) {
+      const float* qa = q[it];
+      const float* ka = k[it];
+      float4* wq0 = reinterpret_cast<float4*>(ws + r * N + o0);
+      float4* wq1 = reinterpret_cast<float4*>(ws + r * N + o1);
+      float4* wk0 = reinterpret_cast<float4*>(ws + R * N + r * N + o0);
+      float4* wk1 = reinterpret_cast<float4*>(ws + R * N + r * N + o1);
+      wq0[0] = make_float4(qa[0], qa[1], qa[2], qa[3]);
+      wq0[1] = make_float4(qa[4], qa[5], qa[6], qa[7]);
+      wq1[0] = make_float4(qa[8], qa[9], qa[10], qa[11]);
+      wq1[1] = make_float4(qa[12], qa[13], qa[14], qa[15]);
+      wk0[0] = make_float4(ka[0], ka[1], ka[2], ka[3]);
+      wk0[1] = make_float4(ka[4], ka[5], ka[6], ka[7]);
+      wk1[0] = make_float4(ka[8], ka[9], ka[10], ka[11]);
+      wk1[1] = make_float4(ka[12], ka[13], ka[14], ka[15]);
+      const m3_tensor& o = a.out_k;
+      T* op = static_cast<T*>(o.data) + b * o.stride[0] + h * o.stride[1] + r * o.stride[2];
+      *reinterpret_cast<uint4*>(op + o0) = pack8<T>(ka);
+      *reinterpret_cast<uint4*>(op + o1) = pack8<T>(ka + 8);
+    }
+  }
+  if (lane == 0) {
+    const float alpha = expf(adtv);
+    const float sg = sigmoidf_(trapv);
+    *reinterpret_cast<float4*>(ws + 2 * R * N) = make_float4(alpha, (1.0f - sg) * dtv * alpha, sg * dtv, Dh);
+  }
+}
+
+// Rows of a [B, H, R, N] 16-bit tensor that are contiguous and start on 16-byte boundaries.
+static bool rows16(const m3_tensor& t) {
+  return t.dtype != M3_F32 && t.stride[3] == 1 && (reinterpret_cast<uintptr_t>(t.data) & 15u) == 0 &&
+         t.stride[0] % 8 == 0 && t.stride[1] % 8 == 0 && t.stride[2] % 8 == 0;
+}
+
 template <typename T, int R, int NV, int RPW>
 __global__ void __launch_bounds__(kStepThreads) step_stream_kernel(const m3_step_args a, int vec_prev_k) {
   const int h = blockIdx.y, b = blockIdx.z;
@@ -490,13 +667,28 @@ __global__ void __launch_bounds__(kStepThreads) step_stream_kernel(const m3_step
     }
   }
   const float4 sc = *reinterpret_cast<const float4*>(ws + 2 * R * N);  // alpha, beta, gamma, D
-  // Per-row inputs: lane rr of the warp loads row p0 + rr.
-  float x_l = 0.f, xp_l = 0.f, z_l = 0.f;
-  if (lane < RPW && p0 + lane < P) {
-    const int p = p0 + lane;
+  // Rank-scattered layout (R in {2, 4}, R * RPW <= 32): lane L stands for rank L / G of row L % G
+  // (G = 32 / R lanes per rank). It holds that row's x mx_r, xp mx_r, z mz_r and mo_r, hands them to
+  // the other lanes by shuffle, receives the row's sum for its rank from a reduce-scatter and runs one
+  // (row, rank) epilogue; the ranks are then summed across lane groups.
+  constexpr bool kScatter = R > 1 && R * RPW <= 32;
+  constexpr int G = 32 / R;
+  const int lrow = kScatter ? lane % G : lane, lrank = kScatter ? lane / G : 0;
+  float x_l = 0.f, xp_l = 0.f, z_l = 0.f, mo_l = 1.f;
+  if (lrow < RPW && p0 + lrow < P) {
+    const int p = p0 + lrow;
     x_l = ld_t(a.value, b * a.value.stride[0] + h * a.value.stride[1] + p * a.value.stride[2]);
     xp_l = ld_t(a.prev_value, b * a.prev_value.stride[0] + h * a.prev_value.stride[1] + p * a.prev_value.stride[2]);
     z_l = ld_t(a.gate, b * a.gate.stride[0] + h * a.gate.stride[1] + p * a.gate.stride[2]);
+    if (kScatter) {
+      const int64_t o = h * a.mimo_x.stride[0] + lrank * a.mimo_x.stride[1] + p * a.mimo_x.stride[2];
+      const float mx = rnd<T>(ld_t(a.mimo_x, o));
+      x_l = rnd<T>(x_l * mx);
+      xp_l = rnd<T>(xp_l * mx);
+      z_l = rnd<T>(z_l * rnd<T>(ld_t(a.mimo_z, h * a.mimo_z.stride[0] + lrank * a.mimo_z.stride[1] +
+                                              p * a.mimo_z.stride[2])));
+      mo_l = ld_t(a.mimo_out, h * a.mimo_out.stride[0] + lrank * a.mimo_out.stride[1] + p * a.mimo_out.stride[2]);
+    }
   }
   float acc_l[R];
 #pragma unroll
@@ -505,17 +697,25 @@ __global__ void __launch_bounds__(kStepThreads) step_stream_kernel(const m3_step
   for (int rr = 0; rr < RPW; ++rr) {
     const int p = p0 + rr;
     if (p >= P) break;  // warp-uniform
-    const float x = __shfl_sync(0xffffffffu, x_l, rr), xp = __shfl_sync(0xffffffffu, xp_l, rr);
     float xv[R], xpv[R];
+    if (kScatter) {
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (R > 1) {
-        const float mx = rnd<T>(ld_t(a.mimo_x, h * a.mimo_x.stride[0] + r * a.mimo_x.stride[1] + p * a.mimo_x.stride[2]));
-        xv[r] = rnd<T>(x * mx);
-        xpv[r] = rnd<T>(xp * mx);
-      } else {
-        xv[r] = x;
-        xpv[r] = xp;
+      for (int r = 0; r < R; ++r) {
+        xv[r] = __shfl_sync(0xffffffffu, x_l, r * G + rr);
+        xpv[r] = __shfl_sync(0xffffffffu, xp_l, r * G + rr);
+      }
+    } else {
+      const float x = __shfl_sync(0xffffffffu, x_l, rr), xp = __shfl_sync(0xffffffffu, xp_l, rr);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (R > 1) {
+          const float mx = rnd<T>(ld_t(a.mimo_x, h * a.mimo_x.stride[0] + r * a.mimo_x.stride[1] + p * a.mimo_x.stride[2]));
+          xv[r] = rnd<T>(x * mx);
+          xpv[r] = rnd<T>(xp * mx);
+        } else {
+          xv[r] = x;
+          xpv[r] = xp;
+        }
       }
     }
     float acc[R];
@@ -546,14 +746,40 @@ __global__ void __launch_bounds__(kStepThreads) step_stream_kernel(const m3_step
                     rnd<T>(ns.w) * qv[r][v].w;
       }
     }
+    if (kScatter) {
+      // Reduce-scatter: each exchange halves the ranks a lane carries (lanes with bit `off` keep the
+      // upper half), then the lanes of a rank group finish the sum; rank r of this row ends in every
+      // lane of group r.
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      acc[r] = warp_sum(acc[r]);
-      if (lane == rr) acc_l[r] = acc[r];  // lane rr finishes row rr below
+      for (int cnt = R, off = 16; cnt > 1; cnt >>= 1, off >>= 1) {
+        const bool up = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < cnt / 2; ++i) {
+          const float send = up ? acc[i] : acc[i + cnt / 2];
+          const float keep = up ? acc[i + cnt / 2] : acc[i];
+          acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+#pragma unroll
+      for (int off = G / 2; off > 0; off >>= 1) acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
+      if (lrow == rr) acc_l[0] = acc[0];
+    } else {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        acc[r] = warp_sum(acc[r]);
+        if (lane == rr) acc_l[r] = acc[r];  // lane rr finishes row rr below
+      }
     }
   }
-  // Row epilogues, one row per lane: y = sum_r mo_r silu(z mz_r) (S' q_r + D x mx_r).
-  if (lane < RPW && p0 + lane < P) {
+  // Row epilogues: y = sum_r mo_r silu(z mz_r) (S' q_r + D x mx_r).
+  const bool row_ok = lrow < RPW && p0 + lrow < P;
+  if (kScatter) {
+    float o = row_ok ? (acc_l[0] + sc.w * x_l) * __fdividef(z_l, 1.0f + __expf(-z_l)) * mo_l : 0.0f;
+#pragma unroll
+    for (int off = G; off < 32; off <<= 1) o += __shfl_xor_sync(0xffffffffu, o, off);
+    if (row_ok && lrank == 0)
+      static_cast<T*>(a.y.data)[b * a.y.stride[0] + h * a.y.stride[1] + (p0 + lrow) * a.y.stride[2]] = from_f<T>(o);
+  } else if (row_ok) {
     const int p = p0 + lane;
     float y = 0.0f;
 #pragma unroll
@@ -576,7 +802,10 @@ static cudaError_t launch_step_two_pass(const m3_step_args& a, cudaStream_t stre
   const int64_t pairs = (int64_t)a.batch * a.heads;
   const int per_cta = kStepThreads / 32;
   const unsigned grid = (unsigned)((pairs + per_cta - 1) / per_cta);
-  if (a.d_state == 128) step_prep_kernel<T, R, 128><<<grid, kStepThreads, 0, stream>>>(a);
+  // Rank 1 keeps the per-pair kernel: its 8 units would leave 24 lanes of each warp idle.
+  if (R > 1 && sizeof(T) == 2 && a.d_state == 128 && rows16(a.q) && rows16(a.k) && rows16(a.out_k))
+    step_prep_vec_kernel<T, R><<<grid, kStepThreads, 0, stream>>>(a);
+  else if (a.d_state == 128) step_prep_kernel<T, R, 128><<<grid, kStepThreads, 0, stream>>>(a);
   else step_prep_kernel<T, R, 0><<<grid, kStepThreads, 0, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
