@@ -100,9 +100,11 @@ __host__ __device__ constexpr int ws_stride(int R, int S) { return ws_ang(R) + (
 template <int R> struct Layout {
   static constexpr int TOK = kRows / R;
   static constexpr int WSP = ws_stride(R, kMaxAngles);
-  // CBq/CBk: packed bias words [R][64]; CMx/CMz/CMo: MIMO projections (float); CMxp: CMx packed [R][32]
+  // CBq/CBk: packed bias words [R][64]; CMx/CMo: MIMO projections (float) [R][64]; CMz: mz packed
+  // [R][32] (in the first half of its slot); CMxp: CMx packed [R][32]
   static constexpr int CBq = kSEnd, CBk = CBq + R * kN, CMx = CBk + R * kN, CMz = CMx + R * kP, CMo = CMz + R * kP;
   static constexpr int CMxp = CMo + R * kP;
+  static_assert(CMz % 4 == 0 && CMo % 4 == 0, "16-byte aligned MIMO parameter rows");
   static constexpr int CWq = CMxp + R * kP / 2, CWk = CWq + kN / 2;   // packed norm weights [64]
   static constexpr int Ws = ((CWk + kN / 2 + 31) / 32) * 32;  // tile's workspace rows [TOK][WSP] (128 B)
   static constexpr int Seg = Ws + TOK * WSP;            // [kWarps][32] sums, then [kWarps][32] offsets
@@ -621,9 +623,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int i = tid; i < R * kP; i += kThreads) {
       const int r = i / kP, p = i % kP;
       cst[Lay::CMx + i] = ld_t(a.mimo_x, h * a.mimo_x.stride[0] + r * a.mimo_x.stride[1] + p * a.mimo_x.stride[2]);
-      cst[Lay::CMz + i] = ld_t(a.mimo_z, h * a.mimo_z.stride[0] + r * a.mimo_z.stride[1] + p * a.mimo_z.stride[2]);
       cst[Lay::CMo + i] =
           ld_t(a.mimo_out, h * a.mimo_out.stride[0] + r * a.mimo_out.stride[1] + p * a.mimo_out.stride[2]);
+    }
+    // mz packed [R][32]: the gate product z mz is rounded to the activation dtype, as the reference's
+    // `gate * mimo_z.to(gate.dtype)` is.
+    uint32_t* cmzp = reinterpret_cast<uint32_t*>(cst + Lay::CMz);
+    for (int i = tid; i < R * kP / 2; i += kThreads) {
+      const int r = i / (kP / 2), p = 2 * (i % (kP / 2));
+      const m3_tensor& mz = a.mimo_z;
+      cmzp[i] = pack2<T>(ld_t(mz, h * mz.stride[0] + r * mz.stride[1] + p * mz.stride[2]),
+                         ld_t(mz, h * mz.stride[0] + r * mz.stride[1] + (p + 1) * mz.stride[2]));
     }
     uint32_t* cmxp = reinterpret_cast<uint32_t*>(cst + Lay::CMxp);
     for (int i = tid; i < R * kP / 2; i += kThreads) {
@@ -1172,34 +1182,74 @@ __global__ void __launch_bounds__(kThreads, 2)
             out[jj] = y0 * g.x;
             out[jj + 1] = y1 * g.y;
           } else {
-            const float2 z = unpack2<T>(zw[e]);
-            const int p = p0 + jj;
-            const float za = z.x * cst[Lay::CMz + r * kP + p], zb = z.y * cst[Lay::CMz + r * kP + p + 1];
-            out[jj] = y0 * __fdividef(za, 1.0f + __expf(-za)) * cst[Lay::CMo + r * kP + p];
-            out[jj + 1] = y1 * __fdividef(zb, 1.0f + __expf(-zb)) * cst[Lay::CMo + r * kP + p + 1];
+            const uint32_t mzw = reinterpret_cast<const uint32_t*>(cst + Lay::CMz)[r * (kP / 2) + (p0 + jj) / 2];
+            const float2 g = unpack2<T>(silu2<T>(mul2<T>(zw[e], mzw)));
+            out[jj] = y0 * g.x;
+            out[jj + 1] = y1 * g.y;
           }
         }
       }
-      if (R > 1) {
+      if (R == 1) {
+        if (valid) {
+          const int t = scan_token(a, t0 + ti);
+          const int64_t ob = b * a.y.stride[0] + (int64_t)t * a.y.stride[1] + h * a.y.stride[2] +
+                             (int64_t)p0 * a.y.stride[3];
+          if (vec_y) {
+            uint4* dst = reinterpret_cast<uint4*>(yp + ob);
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
+            for (int c = 0; c < 2; ++c)
+              dst[c] = make_uint4(pack2<T>(out[8 * c], out[8 * c + 1]), pack2<T>(out[8 * c + 2], out[8 * c + 3]),
+                                  pack2<T>(out[8 * c + 4], out[8 * c + 5]), pack2<T>(out[8 * c + 6], out[8 * c + 7]));
+          } else {
 #pragma unroll
-          for (int o = 1; o < R; o <<= 1) out[jj] += __shfl_xor_sync(0xffffffffu, out[jj], o);
+            for (int jj = 0; jj < 16; ++jj) yp[ob + jj * a.y.stride[3]] = from_f<T>(out[jj]);
+          }
         }
-      }
-      if (valid && r == 0) {
-        const int t = scan_token(a, t0 + ti);
-        const int64_t ob = b * a.y.stride[0] + (int64_t)t * a.y.stride[1] + h * a.y.stride[2] +
-                           (int64_t)p0 * a.y.stride[3];
-        if (vec_y) {
-          uint4* dst = reinterpret_cast<uint4*>(yp + ob);
+      } else {
+        // times mo_r, then the rank sum as a reduce-scatter over the R adjacent lanes of a token: each
+        // exchange halves the columns a lane carries (the lane with bit `o` keeps the upper half), so
+        // lane r ends with 16 / R finished columns starting at p0 + cb.
+        const float4* mo4 = reinterpret_cast<const float4*>(cst + Lay::CMo + r * kP + p0);
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-            dst[c] = make_uint4(pack2<T>(out[8 * c], out[8 * c + 1]), pack2<T>(out[8 * c + 2], out[8 * c + 3]),
-                                pack2<T>(out[8 * c + 4], out[8 * c + 5]), pack2<T>(out[8 * c + 6], out[8 * c + 7]));
-        } else {
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 m = mo4[q4];
+          out[4 * q4] *= m.x;
+          out[4 * q4 + 1] *= m.y;
+          out[4 * q4 + 2] *= m.z;
+          out[4 * q4 + 3] *= m.w;
+        }
+        int cb = 0;
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) yp[ob + jj * a.y.stride[3]] = from_f<T>(out[jj]);
+        for (int o = 1, cnt = 16; o < R; o <<= 1, cnt >>= 1) {
+          const bool up = (lane & o) != 0;
+#pragma unroll
+          for (int i = 0; i < cnt / 2; ++i) {
+            const float send = up ? out[i] : out[i + cnt / 2];
+            const float keep = up ? out[i + cnt / 2] : out[i];
+            out[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+          }
+          if (up) cb += cnt / 2;
+        }
+        constexpr int kCols = 16 / R;
+        if (valid) {
+          const int t = scan_token(a, t0 + ti);
+          const int64_t ob = b * a.y.stride[0] + (int64_t)t * a.y.stride[1] + h * a.y.stride[2] +
+                             (int64_t)(p0 + cb) * a.y.stride[3];
+          if (vec_y && kCols >= 2) {
+            uint32_t w[kCols / 2];
+#pragma unroll
+            for (int i = 0; i < kCols / 2; ++i) w[i] = pack2<T>(out[2 * i], out[2 * i + 1]);
+            if constexpr (kCols == 8) {
+              *reinterpret_cast<uint4*>(yp + ob) = make_uint4(w[0], w[1], w[2], w[3]);
+            } else if constexpr (kCols == 4) {
+              *reinterpret_cast<uint2*>(yp + ob) = make_uint2(w[0], w[1]);
+            } else {
+              *reinterpret_cast<uint32_t*>(yp + ob) = w[0];
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < kCols; ++jj) yp[ob + jj * a.y.stride[3]] = from_f<T>(out[jj]);
+          }
         }
       }
     }
