@@ -194,32 +194,67 @@ class _Mamba3Mixer(nn.Module):
 
     # ---- forward ----------------------------------------------------------------------------
 
-    def _scan_fused(self, projected: torch.Tensor, cache: _LayerCache | None, *, reverse: bool, want_cache: bool):
-        """One kernel launch for the whole SSD of this mixer (one direction), from raw projections."""
+    def _scan_fused(self, projected: torch.Tensor, cache: _LayerCache | None, *, reverse: bool, want_cache: bool,
+                    heads: tuple[int, int] | None = None):
+        """One kernel launch for the whole SSD of this mixer (one direction), from raw projections.
+        ``heads = (h0, h1)`` restricts it to those heads (head sharding): the per-head columns and
+        parameters are sliced as views, q/k/angles are shared by every head."""
         z, x, B, C, delta, decay, trap, angles = self._views(projected)
+        h0, h1 = heads if heads is not None else (0, self.nheads)
+        hs = slice(h0, h1)
+        nh = h1 - h0
+
+        def per_head(t):
+            return None if t is None else t[hs]
+
+        if heads is not None:
+            z, x, delta, decay, trap = z[:, :, hs], x[:, :, hs], delta[..., hs], decay[..., hs], trap[..., hs]
         batch, length = projected.shape[:2]
         act = projected.dtype
-        y = torch.empty(batch, length, self.nheads, self.headdim, device=projected.device, dtype=act)
-        state = torch.empty(batch, self.nheads, self.headdim, self.d_state, device=projected.device,
-                            dtype=torch.float32)
+        y = torch.empty(batch, length, nh, self.headdim, device=projected.device, dtype=act)
+        state = torch.empty(batch, nh, self.headdim, self.d_state, device=projected.device, dtype=torch.float32)
         final_phase = final_k = None
         if want_cache:
-            final_phase = torch.empty(batch, self.nheads, self.num_angles, device=projected.device,
-                                      dtype=torch.float32)
-            final_k = torch.empty(batch, self.nheads, self.mimo_rank, self.d_state, device=projected.device, dtype=act)
-        tensors = dict(q=C, k=B, q_norm_w=self.C_norm.weight, k_norm_w=self.B_norm.weight, q_bias=self.C_bias,
-                       k_bias=self.B_bias, value=x, gate=z, adt=decay, dt=delta, trap=trap, dt_bias=self.dt_bias,
-                       angles=angles, D=self.D, mimo_x=self.mimo_x, mimo_z=self.mimo_z, mimo_out=self.mimo_out,
-                       y=y, final_state=state, final_phase=final_phase, final_k=final_k)
+            final_phase = torch.empty(batch, nh, self.num_angles, device=projected.device, dtype=torch.float32)
+            final_k = torch.empty(batch, nh, self.mimo_rank, self.d_state, device=projected.device, dtype=act)
+        tensors = dict(q=C, k=B, q_norm_w=self.C_norm.weight, k_norm_w=self.B_norm.weight,
+                       q_bias=per_head(self.C_bias), k_bias=per_head(self.B_bias), value=x, gate=z, adt=decay,
+                       dt=delta, trap=trap, dt_bias=per_head(self.dt_bias), angles=angles, D=per_head(self.D),
+                       mimo_x=per_head(self.mimo_x), mimo_z=per_head(self.mimo_z),
+                       mimo_out=per_head(self.mimo_out), y=y, final_state=state, final_phase=final_phase,
+                       final_k=final_k)
         if cache is not None:
             tensors.update(initial_phase=cache[0], initial_state=cache[1], initial_k=cache[2].to(act),
                            initial_value=cache[3].to(act))
-        sizes = dict(batch=batch, length=length, groups=self.ngroups, heads=self.nheads, rank=self.mimo_rank,
+        sizes = dict(batch=batch, length=length, groups=self.ngroups, heads=nh, rank=self.mimo_rank,
                      d_state=self.d_state, head_dim=self.headdim, num_angles=self.num_angles)
         _ext.scan_forward(sizes=sizes, tensors=tensors, reverse=reverse, mimo_rotation=self.mimo_rank > 1,
                           chunk_hint=self.inference_chunk_size, norm_eps=self.C_norm.eps)
         ops.LAST_SCAN_DISPATCH = True
         return y, state, final_phase, final_k, x
+
+    def mixed_heads(self, hidden_states: torch.Tensor, h0: int, h1: int, *, reverse: bool = False) -> torch.Tensor:
+        """SSD output ``[B, L, h1 - h0, P]`` (before out_proj) of heads ``[h0, h1)`` for one direction:
+        the unit of head sharding. The projection is computed in full (B/C and the angles are shared
+        by every head); only the scan is restricted. ``reverse`` scans back to front (the second
+        direction of a bidirectional mixer) and returns rows in the original order."""
+        if not 0 <= h0 < h1 <= self.nheads:
+            raise ValueError(f"head range [{h0}, {h1}) outside [0, {self.nheads})")
+        if self._use_kernels(hidden_states):
+            projected = self._project_linear("in_proj", hidden_states)
+            return self._scan_fused(projected, None, reverse=reverse, want_cache=False, heads=(h0, h1))[0]
+        hidden = torch.flip(hidden_states, dims=(1,)) if reverse else hidden_states
+        q, k, x, z, adt, dt, trap, angles = self._project(hidden)
+        phase = self._phase(angles, dt, None)
+        hs = slice(h0, h1)
+        chunk = self.chunk_size if self.training and torch.is_grad_enabled() else self.inference_chunk_size
+        per_head = (lambda t: None if t is None else t[hs])
+        mixed, _ = mamba3_scan(
+            q, k, x[:, :, hs], z[:, :, hs], adt[..., hs], dt[..., hs], trap[..., hs], self.D[hs],
+            mimo_x=per_head(self.mimo_x), mimo_z=per_head(self.mimo_z), mimo_out=per_head(self.mimo_out),
+            chunk_size=chunk, phase=phase[:, :, hs], mimo_rotation=self.mimo_rank > 1, q_bias=self.C_bias[hs],
+            k_bias=self.B_bias[hs])
+        return torch.flip(mixed, dims=(1,)) if reverse else mixed
 
     def _use_kernels(self, hidden_states: torch.Tensor) -> bool:
         return _kernel_eligible(hidden_states, *self.parameters())

@@ -42,3 +42,49 @@ def forward_sharded(model, x: torch.Tensor, group=None) -> torch.Tensor:
         s, e = shard_bounds(batch, world, r)
         pieces.append(part[: e - s])
     return torch.cat(pieces, dim=0)
+
+
+def _gather_heads(local: torch.Tensor, heads: int, world: int, group) -> torch.Tensor:
+    """All-gather ``[B, L, h_r, P]`` head shards (near-equal split of ``heads``) into ``[B, L, heads, P]``."""
+    widest = -(-heads // world)
+    padded = local.new_zeros((*local.shape[:2], widest, local.shape[3]))
+    padded[:, :, : local.shape[2]] = local
+    parts = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(parts, padded.contiguous(), group=group)
+    pieces = []
+    for r, part in enumerate(parts):
+        s, e = shard_bounds(heads, world, r)
+        pieces.append(part[:, :, : e - s])
+    return torch.cat(pieces, dim=2)
+
+
+def forward_head_sharded(model, x: torch.Tensor, group=None) -> torch.Tensor:
+    """``model(x)`` with the heads of every mixer split across ranks: the fallback when the batch is
+    smaller than the number of GPUs (batch 1 prefill).
+
+    Each rank computes the replicated parts (norms, in_proj, out_proj, residual) in full and the scan
+    of its contiguous share of the heads; one all-gather of the mixer output ``[B, L, H, P]`` along
+    heads per layer and direction precedes out_proj. Every rank passes the same ``x`` and receives
+    the full output.
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    for layer in model.layers:
+        mixer = layer.mixer
+        h0, h1 = shard_bounds(mixer.nheads, world, rank)
+        hidden = layer.norm(x)
+
+        def direction(reverse: bool) -> torch.Tensor:
+            if h1 > h0:
+                local = mixer.mixed_heads(hidden, h0, h1, reverse=reverse)
+            else:  # more ranks than heads: an empty share still joins the gather
+                local = hidden.new_empty((*hidden.shape[:2], 0, mixer.headdim))
+            mixed = _gather_heads(local, mixer.nheads, world, group)
+            return mixer._project_linear("out_proj", mixed.flatten(-2))
+
+        out = direction(False)
+        if not mixer.causal:
+            blend = torch.sigmoid(mixer.direction_logit).to(out.dtype)
+            out = out * blend + direction(True) * (1.0 - blend)
+        x = x + out
+    return model.norm_f(x)

@@ -259,3 +259,22 @@ def test_autocast_weight_cast_cache_is_exact_and_invalidated():
     updated = run()
     assert rel_err(updated, first) > 1e-3
     torch.testing.assert_close(fresh(), updated, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("rank,causal", [(1, True), (4, True), (1, False)])
+def test_head_range_scans_match_the_full_scan(rank, causal):
+    """Head sharding on the kernel path: the tensor-core scan restricted to head ranges (sliced
+    per-head columns and parameters, shared q/k/angles) reproduces the full scan's heads bit for bit."""
+    torch.manual_seed(12)
+    model = Mamba3(256, d_state=128, depth=1, mimo_rank=rank, causal=causal).cuda().eval()
+    mixer = model.layers[0].mixer
+    x = torch.randn(1, 300, 256, device="cuda")
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        hidden = model.layers[0].norm(x)
+        projected = mixer._project_linear("in_proj", hidden)
+        for reverse in ((False, True) if not causal else (False,)):
+            full = mixer._scan_fused(projected, None, reverse=reverse, want_cache=False)[0]
+            assert _ext.last_scan_kernel() == "umma"
+            parts = torch.cat([mixer.mixed_heads(hidden, 0, 3, reverse=reverse),
+                               mixer.mixed_heads(hidden, 3, mixer.nheads, reverse=reverse)], dim=2)
+            torch.testing.assert_close(parts, full, rtol=0, atol=0)
