@@ -44,7 +44,9 @@ DECODE = dict(d_model=2560, depth=32, batch=64)
 # DRAM bytes (read + write) per token of one scan-kernel launch, from one ncu capture of the same
 # kernel on a smaller case of the workload (dram__bytes_read.sum + dram__bytes_write.sum = 192.33 MB
 # over 2 x 8192 tokens, d_model 1024, rank 1). Traffic grows with tokens, so the bench scales it.
-SCAN_TRAFFIC_PER_TOKEN = {"siso": 192.33e6 / 16384}
+SCAN_TRAFFIC_PER_TOKEN = {"siso": 192.33e6 / 16384,
+                          # d_model 2048, rank 4: 156.67 + 47.51 MB over 2 x 4096 tokens
+                          "mimo": 204.18e6 / 8192}
 
 
 def peaks() -> tuple[dict, str]:
@@ -233,7 +235,7 @@ def run_prefill(args, world, rank, local):
     # fused residual add + RMSNorm
     launches_per_step = depth * 2 * (1 if causal else 2) + depth + 1  # + residual add / RMSNorm kernels
     traffic = (SCAN_TRAFFIC_PER_TOKEN[args.workload] * batch * length
-               if args.workload in SCAN_TRAFFIC_PER_TOKEN and mrank == 1 and d_model == 1024 else None)
+               if args.workload in SCAN_TRAFFIC_PER_TOKEN else None)
     common = {"peak_kind": pk_kind, "kernel": f"m3 scan ({kernel_name})", "kernel_ms": kernel_ms,
               "algorithmic_bytes_per_launch": bytes_launch, "algorithmic_flops_per_launch": flops_launch}
     if mrank > 1:  # arithmetic intensity above the ridge: graded on the tensor pipe
