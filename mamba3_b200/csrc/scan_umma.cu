@@ -413,7 +413,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   float* edec = fsm + kSEdec;
   float* scale = fsm + kSScale;
   float* diag = fsm + kSDiag;
-  float* sdt = fsm + kSDt;
   float* wsum = fsm + kSWsum;
   float* cum_l2 = fsm + kSCumL2;
   float* fq = fsm + kSFq;
@@ -780,7 +779,6 @@ __global__ void __launch_bounds__(kThreads, 2)
           o_ec[m] = v ? (fct ? __expf(cmid) : __expf(c)) : 0.0f;
           o_ed[m] = (v && !fct) ? __expf(cl - c) : 0.0f;
         }
-        *reinterpret_cast<float2*>(sdt + j0) = make_float2(dtv[0], dtv[1]);
         *reinterpret_cast<float2*>(cum_l2 + j0) = make_float2(cum2[0] * kLog2e, cum2[1] * kLog2e);
         *reinterpret_cast<float2*>(diag + j0) = make_float2(dg[0], dg[1]);
         *reinterpret_cast<float2*>(fq + j0) = make_float2(o_fq[0], o_fq[1]);
@@ -795,7 +793,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         mode[3] = __expf(cl);
       }
     }
-    __syncthreads();
+    // No barrier: the phase section below reads only sraw (dt) and the workspace rows, so warps 1-7
+    // start on their angles while warp 0 finishes the scalars; the barrier after the phases covers both.
     M3_MARK(2);
     // ---- phases -> packed (cos, sin) words over pi*tanh(angle) in wsb. Warp w: angles 4 w .. 4 w + 3
     // (carried block offset and in-block sum in registers, mamba3/model.py:246-251); lane: tokens
@@ -821,7 +820,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             float dtj = 0.0f;
             if (j < nt) {
               av = *reinterpret_cast<const float4*>(wsb + j * WS + WA + s0);
-              dtj = sdt[j];
+              dtj = sraw[j];  // dt of token j (finish_scalars), not waiting for the scalar section
             }
             const float in[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
