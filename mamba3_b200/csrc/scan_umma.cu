@@ -709,11 +709,18 @@ __global__ void __launch_bounds__(kThreads, 2)
   for (int k_ = 0; k_ < 16; ++k_) mark_acc_[k_] = 0;
 #endif
 
-  // Phase carry of this warp's angles 4 warp .. 4 warp + 3 (block offset, in-block sum).
-  float ph_off[4], ph_loc[4];
+  // Phase carry of this warp's angles (block offset, in-block sum). Rank 1 (64 tokens per tile): every
+  // warp owns kPhA = 4 angles, s0 = 4 warp. Rank > 1 (at most 32 tokens, so a warp's scans are short):
+  // warps 1 .. 6 own 6 angles each, s0 = 6 (warp - 1) (36 slots >= kMaxAngles), and warp 0, which
+  // computes the per-token scalars meanwhile, has none (nor has warp 7).
+  constexpr int kPhA = R == 1 ? 4 : 6;
+  static_assert((R == 1 ? kWarps : 6) * kPhA >= kMaxAngles && kPhA % 2 == 0,
+                "phase warps must cover every angle in pairs");
+  const int ph_s0 = R == 1 ? kPhA * warp : ((warp >= 1 && warp <= 6) ? kPhA * (warp - 1) : kMaxAngles);
+  float ph_off[kPhA], ph_loc[kPhA];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int sidx = 4 * warp + k;
+  for (int k = 0; k < kPhA; ++k) {
+    const int sidx = ph_s0 + k;
     ph_off[k] = (a.initial_phase.data && sidx < S)
                     ? ld_t(a.initial_phase, b * a.initial_phase.stride[0] + h * a.initial_phase.stride[1] +
                                                 sidx * a.initial_phase.stride[2])
@@ -796,38 +803,51 @@ __global__ void __launch_bounds__(kThreads, 2)
     // No barrier: the phase section below reads only sraw (dt) and the workspace rows, so warps 1-7
     // start on their angles while warp 0 finishes the scalars; the barrier after the phases covers both.
     M3_MARK(2);
-    // ---- phases -> packed (cos, sin) words over pi*tanh(angle) in wsb. Warp w: angles 4 w .. 4 w + 3
-    // (carried block offset and in-block sum in registers, mamba3/model.py:246-251); lane: tokens
-    // 2 lane, 2 lane + 1. SISO: word m = (cos_m, sin_m); MIMO (S == 32): word q < 16 = (cos_2q, cos_2q+1),
-    // word 16 + q = (sin_2q, sin_2q+1), the element pairs a staging word holds. ----
+    // ---- phases -> packed (cos, sin) words over pi*tanh(angle) in wsb. A warp's angles s0 .. s0 + kPhA - 1
+    // (carried block offset and in-block sum in registers,
+    // mamba3/model.py:246-251); lane: tokens 2 lane, 2 lane + 1. SISO: word m = (cos_m, sin_m); MIMO
+    // (S == 32): word q < 16 = (cos_2q, cos_2q+1), word 16 + q = (sin_2q, sin_2q+1), the element
+    // pairs a staging word holds. ----
     if (has_phase) {
-      const int s0 = 4 * warp, j0 = 2 * lane;
-      float ph[2][4];
+      const int s0 = ph_s0, j0 = 2 * lane;
+      float ph[2][kPhA];
       if (s0 < S) {
         if (a.angles.data) {
           if (t0 > 0 && (t0 % kPhaseBlock) == 0) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < kPhA; ++k) {
               ph_off[k] = fmodf(ph_off[k] + ph_loc[k], kTwoPi);
               ph_loc[k] = 0.0f;
             }
           }
-          float inc[2][4];
+          float inc[2][kPhA];
 #pragma unroll
           for (int m = 0; m < 2; ++m) {
             const int j = j0 + m;
-            float4 av = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float in[kPhA] = {};
             float dtj = 0.0f;
             if (j < nt) {
-              av = *reinterpret_cast<const float4*>(wsb + j * WS + WA + s0);
+              if constexpr (kPhA == 4) {  // s0 = 4 warp: one 16-byte load
+                const float4 av = *reinterpret_cast<const float4*>(wsb + j * WS + WA + s0);
+                in[0] = av.x;
+                in[1] = av.y;
+                in[2] = av.z;
+                in[3] = av.w;
+              } else {
+#pragma unroll
+                for (int k2 = 0; k2 < kPhA / 2; ++k2) {
+                  const float2 av = *reinterpret_cast<const float2*>(wsb + j * WS + WA + s0 + 2 * k2);
+                  in[2 * k2] = av.x;
+                  in[2 * k2 + 1] = av.y;
+                }
+              }
               dtj = sraw[j];  // dt of token j (finish_scalars), not waiting for the scalar section
             }
-            const float in[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) inc[m][k] = s0 + k < S ? fmod_2pi(in[k] * dtj) : 0.0f;
+            for (int k = 0; k < kPhA; ++k) inc[m][k] = s0 + k < S ? fmod_2pi(in[k] * dtj) : 0.0f;
           }
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
+          for (int k = 0; k < kPhA; ++k) {
             const float x = warp_incl_scan(inc[0][k] + inc[1][k], lane);
             const float tot = __shfl_sync(0xffffffffu, x, 31);
             ph[0][k] = fmod_2pi((ph_loc[k] + (x - inc[1][k])) + ph_off[k]);
@@ -838,12 +858,13 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int m = 0; m < 2; ++m) {
             const int j = j0 + m;
-            float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (j < TOK) pv = *reinterpret_cast<const float4*>(wsb + j * WS + WA + s0);
-            ph[m][0] = pv.x;
-            ph[m][1] = pv.y;
-            ph[m][2] = pv.z;
-            ph[m][3] = pv.w;
+#pragma unroll
+            for (int k2 = 0; k2 < kPhA / 2; ++k2) {
+              float2 pv = make_float2(0.0f, 0.0f);
+              if (j < TOK) pv = *reinterpret_cast<const float2*>(wsb + j * WS + WA + s0 + 2 * k2);
+              ph[m][2 * k2] = pv.x;
+              ph[m][2 * k2 + 1] = pv.y;
+            }
           }
         }
       }
@@ -853,28 +874,40 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int m = 0; m < 2; ++m) {
           const int j = j0 + m;
           if (j < TOK) {
-            float cs[4], sn[4];
+            float cs[kPhA], sn[kPhA];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) __sincosf(ph[m][k], &sn[k], &cs[k]);  // |phase| < 2 pi
+            for (int k = 0; k < kPhA; ++k) __sincosf(ph[m][k], &sn[k], &cs[k]);  // |phase| < 2 pi
             if (t0 + j == L - 1 && a.final_phase.data) {
               const m3_tensor& fp = a.final_phase;
 #pragma unroll
-              for (int k = 0; k < 4; ++k)
+              for (int k = 0; k < kPhA; ++k)
                 if (s0 + k < S)
                   static_cast<float*>(fp.data)[b * fp.stride[0] + h * fp.stride[1] + (s0 + k) * fp.stride[2]] =
                       ph[m][k];
             }
             uint32_t* w = reinterpret_cast<uint32_t*>(wsb + j * WS + WA);
             if (a.mimo_rotation) {
-              *reinterpret_cast<uint2*>(w + s0 / 2) = make_uint2(pack2<T>(cs[0], cs[1]), pack2<T>(cs[2], cs[3]));
-              *reinterpret_cast<uint2*>(w + 16 + s0 / 2) = make_uint2(pack2<T>(sn[0], sn[1]), pack2<T>(sn[2], sn[3]));
-            } else if (s0 + 4 <= S) {
+#pragma unroll
+              for (int k2 = 0; k2 < kPhA / 2; ++k2) {
+                if (s0 + 2 * k2 < S) {
+                  w[s0 / 2 + k2] = pack2<T>(cs[2 * k2], cs[2 * k2 + 1]);
+                  w[16 + s0 / 2 + k2] = pack2<T>(sn[2 * k2], sn[2 * k2 + 1]);
+                }
+              }
+            } else if (kPhA == 4 && s0 + 4 <= S) {
               *reinterpret_cast<uint4*>(w + s0) = make_uint4(pack2<T>(cs[0], sn[0]), pack2<T>(cs[1], sn[1]),
                                                              pack2<T>(cs[2], sn[2]), pack2<T>(cs[3], sn[3]));
             } else {
 #pragma unroll
-              for (int k = 0; k < 4; ++k)
-                if (s0 + k < S) w[s0 + k] = pack2<T>(cs[k], sn[k]);
+              for (int k2 = 0; k2 < kPhA / 2; ++k2) {
+                const int sa = s0 + 2 * k2;
+                if (sa + 1 < S) {
+                  *reinterpret_cast<uint2*>(w + sa) =
+                      make_uint2(pack2<T>(cs[2 * k2], sn[2 * k2]), pack2<T>(cs[2 * k2 + 1], sn[2 * k2 + 1]));
+                } else if (sa < S) {
+                  w[sa] = pack2<T>(cs[2 * k2], sn[2 * k2]);
+                }
+              }
             }
           }
         }
