@@ -830,7 +830,10 @@ bool step_vec_ok(const m3_step_args& a) {
 template <typename T, int R>
 static cudaError_t launch_step_r(const m3_step_args& a, cudaStream_t stream) {
   const int N = a.d_state, P = a.head_dim;
-  if (a.workspace.data != nullptr) {  // set exactly when step_vec_ok (m3_step_workspace_bytes)
+  // Fewer (batch, head) pairs than two per SM: one launch (the single-pass kernel, each CTA repeating
+  // its head's prologue) is shorter than the prep + stream pair, whose cost there is launch latency.
+  const bool few = (long long)a.batch * a.heads < 2 * 148;
+  if (a.workspace.data != nullptr && !few) {  // set exactly when step_vec_ok (m3_step_workspace_bytes)
     // kStepBigRows rows per warp once there are enough (batch, head) pairs to fill
     // the GPU several times; otherwise 2 rows per warp so that even batch 1 spreads over all SMs.
     const bool big = (long long)a.batch * a.heads >= 4 * 148;
