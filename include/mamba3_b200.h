@@ -157,7 +157,8 @@ int m3_residual_rmsnorm(const m3_norm_args* args, void* stream);
 /* Chunked SSD forward. Returns M3_OK or an M3_ERR_* code. */
 int m3_scan_fwd(const m3_scan_args* args, void* stream);
 
-/* Bytes of float32 workspace m3_scan_fwd needs for these arguments (0 = none). */
+/* Bytes of float32 workspace m3_scan_fwd needs for these arguments (0 = none); a negative value
+ * is minus an M3_ERR_* code (null arguments, non-positive sizes) with m3_last_error() set. */
 int64_t m3_scan_workspace_bytes(const m3_scan_args* args);
 
 /* Fixed scratch size of m3_scan_fwd_noalloc, per GPU that loads the library: 8 MiB. */
@@ -171,8 +172,10 @@ int64_t m3_scan_workspace_bytes(const m3_scan_args* args);
  * M3_NOALLOC_WORKSPACE_BYTES per GPU, held until process exit. Sizes whose scratch
  * (m3_scan_workspace_bytes) exceeds that limit are rejected with M3_ERR_SHAPE. The first call on
  * a device looks up the array's device address once; make that first call before any stream
- * capture. All calls share the one array, so calls on one device that overlap on the GPU race on
- * it; calls ordered on one stream are safe. Has no counterpart in the reference.
+ * capture. The address is cached for the life of the process, so the entry point must not be
+ * used on a device after cudaDeviceReset() of that device. All calls share the one array, so calls
+ * on one device that overlap on the GPU race on it; calls ordered on one stream are safe. Has no
+ * counterpart in the reference.
  */
 int m3_scan_fwd_noalloc(const m3_scan_args* args, void* stream);
 
@@ -195,6 +198,11 @@ int m3_device_error(int clear);
 /* Name of the scan kernel variant the last m3_scan_fwd on this thread launched
  * ("umma" for the tcgen05 tensor-core kernel, "simt" for the FP32 CUDA-core kernel). */
 const char* m3_last_scan_kernel(void);
+
+/* Name of the decode-step kernel variant the last m3_step_fwd on this thread launched:
+ * "single" (one launch per step, each CTA repeating its head's prologue), "two_pass" (per-(batch,
+ * head) prep pass + state stream pass) or "two_pass_vec" (the 16-byte-row MIMO prep + stream pass). */
+const char* m3_last_step_kernel(void);
 
 #ifdef __cplusplus
 }

@@ -109,6 +109,8 @@ def load() -> ctypes.CDLL:
         lib.m3_residual_rmsnorm.restype = ctypes.c_int
         lib.m3_last_scan_kernel.argtypes = []
         lib.m3_last_scan_kernel.restype = ctypes.c_char_p
+        lib.m3_last_step_kernel.argtypes = []
+        lib.m3_last_step_kernel.restype = ctypes.c_char_p
         if lib.m3_abi_version() != ABI_VERSION:
             raise RuntimeError("mamba3_b200 library ABI mismatch; rebuild it")
         _lib = lib
@@ -219,6 +221,10 @@ def residual_rmsnorm(x: torch.Tensor, m: torch.Tensor | None, w: torch.Tensor, e
 
 def last_scan_kernel() -> str:
     return load().m3_last_scan_kernel().decode()
+
+
+def last_step_kernel() -> str:
+    return load().m3_last_step_kernel().decode()
 
 
 def device_error(clear: bool = True) -> int:

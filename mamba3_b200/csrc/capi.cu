@@ -9,6 +9,7 @@ namespace m3 {
 int read_device_error(int clear);
 
 cudaError_t launch_step(const m3_step_args& a, cudaStream_t stream);
+const char* last_step_kernel();
 int64_t step_workspace_bytes(const m3_step_args& a);
 cudaError_t launch_scan_simt(const m3_scan_args& a, cudaStream_t stream);
 size_t scan_simt_smem_bytes(int rank, int N, int P, int S);
@@ -70,6 +71,8 @@ const char* m3_last_error(void) { return g_last_error.c_str(); }
 int m3_abi_version(void) { return M3_ABI_VERSION; }
 
 const char* m3_last_scan_kernel(void) { return g_last_scan_kernel; }
+
+const char* m3_last_step_kernel(void) { return m3::last_step_kernel(); }
 
 int m3_device_error(int clear) { return m3::read_device_error(clear); }
 
@@ -136,7 +139,10 @@ int m3_step_fwd(const m3_step_args* args, void* stream) {
 
 int64_t m3_scan_workspace_bytes(const m3_scan_args* args) {
   if (args == nullptr) return -fail(M3_ERR_ARGUMENT, "null argument struct");
-  return m3::scan_umma_supported(*args) ? m3::scan_umma_workspace_bytes(*args) : 0;
+  const m3_scan_args& a = *args;
+  if (a.batch <= 0 || a.length <= 0 || a.heads <= 0 || a.groups <= 0 || a.rank <= 0 || a.num_angles < 0)
+    return -fail(M3_ERR_SHAPE, "batch, length, heads, groups and rank must be positive");
+  return m3::scan_umma_supported(a) ? m3::scan_umma_workspace_bytes(a) : 0;
 }
 
 int m3_scan_fwd(const m3_scan_args* args, void* stream) {

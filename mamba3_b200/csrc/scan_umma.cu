@@ -427,6 +427,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   // Forward scans load their row tiles with TMA (three boxes groups per tile complete on tma_bar);
   // reverse scans, whose tiles run backwards through memory, use per-row asynchronous copies.
   const uint32_t tma_bar = smem_u32(smem + Lay::OffBar + 24);
+  // MMA completion: bar_addr tracks the scores MMAs, bar_b the inter + state-update MMAs issued after
+  // them, bar_c the intra MMAs; each completes one phase per tile.
+  const uint32_t bar_b = smem_u32(smem + Lay::OffBar + 32);
+  const uint32_t bar_c = smem_u32(smem + Lay::OffBar + 40);
   const bool use_tma = !a.reverse;
   const uint32_t bar_addr = smem_u32(bar);
   const uint32_t sbase = smem_u32(smem);
@@ -590,6 +594,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   if (tid == 0) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_addr));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_b));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar_c));
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 3;" ::"r"(tma_bar));  // q/k, x, z (+ workspace)
     asm volatile("fence.mbarrier_init.release.cluster;");
     *abort_flag = 0;
@@ -1079,7 +1085,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     M3_MARK(5);
 
-    // ---- MMA group 1: scores = Q' K'^T, inter = Q' St, X += K'^T V (or V2) ----
+    // ---- MMA group 1: scores = Q' K'^T (committed on its own, so the W section starts as soon as
+    // they land), then inter = Q' St and X += K'^T V (or V2), which finish behind the W section ----
     if (tid == 0) {
       fence_after();
 #pragma unroll
@@ -1088,6 +1095,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         mma_f16(tmem + kColScores, sdesc(sbase + kOffQ + koff, 16, 1024), sdesc(sbase + kOffK + koff, 16, 1024),
                 id_scores, kk > 0);
       }
+      mma_commit(bar_addr);
 #pragma unroll
       for (int kk = 0; kk < kN / 16; ++kk) {
         const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
@@ -1100,7 +1108,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         mma_f16(tmem + kColState, sdesc(sbase + kOffK + kk * 2048, kRows * 128, 1024),
                 sdesc(sbase + vsrc + kk * 2048, kRows * 128, 1024), id_state, 1);
       }
-      mma_commit(bar_addr);
+      mma_commit(bar_b);
     }
     // While the tensor cores run: the next tile's scalars, workspace rows and z rows (other buffer).
     if (ntn > 0) {
@@ -1110,11 +1118,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // One thread polls the barrier; the others wait at __syncthreads without taking issue slots.
     if (tid == 0 && !mbar_wait(bar_addr, phase_bit)) *abort_flag = 1;
-    phase_bit ^= 1;
     __syncthreads();
     fence_after();
-    // Q'/K' are free now: the next tile's raw q/k rows.
-    if (ntn > 0) issue_qk(t0n, ntn);
     M3_MARK(6);
 
     // ---- W = scores o decay -> smem (16-bit, K-major). Thread: row quad * 16 + (lane & 15), columns
@@ -1174,13 +1179,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         mma_f16(tmem + kColIntra, sdesc(sbase + kOffW + koff, 16, 1024),
                 sdesc(sbase + kOffV + kk * 2048, kRows * 128, 1024), id_nmn, kk > 0);
       }
-      mma_commit(bar_addr);
+      mma_commit(bar_c);
     }
-    if (tid == 0 && !mbar_wait(bar_addr, phase_bit)) *abort_flag = 1;
+    // inter and the state update (issued before the W section) have finished: Q'/K' are free, so
+    // the next tile's raw q/k rows can start.
+    if (tid == 0 && !mbar_wait(bar_b, phase_bit)) *abort_flag = 1;
+    if (use_tma) {
+      if (ntn > 0) issue_qk(t0n, ntn);  // one thread issues the TMA boxes; the others skip
+    }
+    if (tid == 0 && !mbar_wait(bar_c, phase_bit)) *abort_flag = 1;
     phase_bit ^= 1;
     __syncthreads();
     fence_after();
-    // W is free now: the next tile's raw x rows.
+    // Row copies of the next tile's q/k (reverse scans) need every thread, after the barrier.
+    if (!use_tma && ntn > 0) issue_qk(t0n, ntn);
+    // W and V are free now: the next tile's raw x rows.
     if (ntn > 0) issue_x(t0n, ntn);
     cp_async_commit();
     M3_MARK(8);

@@ -797,16 +797,25 @@ __global__ void __launch_bounds__(kStepThreads) step_stream_kernel(const m3_step
   }
 }
 
+// Name of the step kernel variant the last launch_step on this host thread chose.
+thread_local const char* g_last_step_kernel = "none";
+
 template <typename T, int R, int NV, int RPW>
 static cudaError_t launch_step_two_pass(const m3_step_args& a, cudaStream_t stream) {
   const int64_t pairs = (int64_t)a.batch * a.heads;
   const int per_cta = kStepThreads / 32;
   const unsigned grid = (unsigned)((pairs + per_cta - 1) / per_cta);
   // Rank 1 keeps the per-pair kernel: its 8 units would leave 24 lanes of each warp idle.
-  if (R > 1 && sizeof(T) == 2 && a.d_state == 128 && rows16(a.q) && rows16(a.k) && rows16(a.out_k))
+  if (R > 1 && sizeof(T) == 2 && a.d_state == 128 && rows16(a.q) && rows16(a.k) && rows16(a.out_k)) {
+    g_last_step_kernel = "two_pass_vec";
     step_prep_vec_kernel<T, R><<<grid, kStepThreads, 0, stream>>>(a);
-  else if (a.d_state == 128) step_prep_kernel<T, R, 128><<<grid, kStepThreads, 0, stream>>>(a);
-  else step_prep_kernel<T, R, 0><<<grid, kStepThreads, 0, stream>>>(a);
+  } else if (a.d_state == 128) {
+    g_last_step_kernel = "two_pass";
+    step_prep_kernel<T, R, 128><<<grid, kStepThreads, 0, stream>>>(a);
+  } else {
+    g_last_step_kernel = "two_pass";
+    step_prep_kernel<T, R, 0><<<grid, kStepThreads, 0, stream>>>(a);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int rows = RPW * (kStepThreads / 32);
@@ -846,6 +855,7 @@ static cudaError_t launch_step_r(const m3_step_args& a, cudaStream_t stream) {
   const long long pairs = (long long)a.batch * a.heads;
   while (rows > 4 && pairs * ((P + rows - 1) / rows) < 4 * 148) rows >>= 1;
   dim3 grid((P + rows - 1) / rows, a.heads, a.batch);
+  g_last_step_kernel = "single";
   const size_t smem = (128 + 3 * (size_t)R * N + 2 * R) * sizeof(float);
   auto go = [&](auto kern) -> cudaError_t {
     if (smem > 48 * 1024) {
@@ -875,6 +885,8 @@ int64_t step_workspace_bytes(const m3_step_args& a) {
   if (!step_vec_ok(a)) return 0;
   return (int64_t)a.batch * a.heads * (2 * a.rank * a.d_state + 4) * (int64_t)sizeof(float);
 }
+
+const char* last_step_kernel() { return g_last_step_kernel; }
 
 cudaError_t launch_step(const m3_step_args& a, cudaStream_t stream) {
   switch (a.value.dtype) {

@@ -157,14 +157,22 @@ def _scalar_prelude(adt, dt, trap_logits):
 
 def _scan_torch(q, k, value, gate, adt, dt, trap_logits, D, *, mimo_x, mimo_z, mimo_out, chunk_size,
                 initial_state, initial_k, initial_value, phase, mimo_rotation, q_bias, k_bias):
-    """Differentiable chunked SSD in float32 arithmetic (mamba3/ops.py:659-822).
+    """Differentiable chunked SSD with the reference's rounding schedule (mamba3/ops.py:659-822).
 
     Per chunk: inter-chunk term e^{cum} (Q S^T), masked decayed scores (Q (K*scale)^T) o L with
     the gamma/scale diagonal, D skip, SiLU gate, MIMO rank sum; then the state carry
     S <- e^{cum_last} S + V^T (K*scale*e^{cum_last - cum}).
+
+    With bf16/fp16 activations the operands are rounded where the reference rounds them: ``scale``,
+    the biased/rotated q/k, ``k*scale``, ``v*mimo_x`` and ``z*mimo_z`` in the activation dtype
+    (ops.py:665-676, 719-745), the state read as ``state.to(q.dtype)`` (ops.py:754), the weighted
+    scores as ``.to(value.dtype)`` (ops.py:787), ``k_scaled * end_decay.to(act)`` (ops.py:807);
+    every product is accumulated in float32 and the state stays float32. With float32 activations
+    every rounding is the identity.
     """
     batch, length, _, rank, d_state = q.shape
     heads, head_dim = value.shape[2], value.shape[3]
+    act = value.dtype
     qf = _expand_groups(q, heads)
     kf = _expand_groups(k, heads)
     if q_bias is not None:
@@ -172,16 +180,20 @@ def _scan_torch(q, k, value, gate, adt, dt, trap_logits, D, *, mimo_x, mimo_z, m
         kf = kf + k_bias.to(k.dtype)
     if phase is not None:
         qf, kf = rotate_qk(qf, kf, phase, mimo=mimo_rotation)
-    qf, kf = qf.float(), kf.float()
     sig, _, scale, diag = _scalar_prelude(adt, dt, trap_logits)
+    scale_act = scale.to(k.dtype)
     adtf = adt.float()
     dtf = dt.float()
-    rv = _rank_values(value, mimo_x)  # [B, L, H, R, P]
-    rz = _rank_values(gate, mimo_z)
+
+    def rank_act(t, proj):  # [..., H, P] -> [..., H, R, P] in the activation dtype (ops.py:193-199)
+        return t.unsqueeze(-2) if proj is None else t.unsqueeze(-2) * proj.to(t.dtype)
+
+    rv = rank_act(value, mimo_x)  # [B, L, H, R, P]
+    rz = rank_act(gate, mimo_z)
     state = (torch.zeros(batch, heads, head_dim, d_state, device=value.device, dtype=torch.float32)
              if initial_state is None else initial_state.float())
     if initial_k is not None:
-        prev = _rank_values(initial_value, mimo_x)
+        prev = rank_act(initial_value, mimo_x).float()
         coef = dtf[:, 0] * (1.0 - sig[:, 0])
         state = state + coef[..., None, None] * torch.einsum("bhrp,bhrn->bhpn", prev, initial_k.float())
     Dv = D.float()[None, :, None, None]
@@ -193,23 +205,26 @@ def _scan_torch(q, k, value, gate, adt, dt, trap_logits, D, *, mimo_x, mimo_z, m
         rows = w * rank
         cum = torch.cumsum(adtf[:, start:end], dim=1).transpose(1, 2)  # [B, H, w]
         Qc = qf[:, start:end].permute(0, 2, 1, 3, 4).reshape(batch, heads, rows, d_state)
-        Kc = (kf[:, start:end] * scale[:, start:end, :, None, None]).permute(0, 2, 1, 3, 4).reshape(
+        Kc = (kf[:, start:end] * scale_act[:, start:end, :, None, None]).permute(0, 2, 1, 3, 4).reshape(
             batch, heads, rows, d_state)
         Vc = rv[:, start:end].permute(0, 2, 1, 3, 4).reshape(batch, heads, rows, head_dim)
         row_cum = cum.repeat_interleave(rank, dim=-1)  # [B, H, rows]
-        inter = torch.matmul(Qc, state.transpose(-1, -2)) * torch.exp(row_cum).unsqueeze(-1)
-        scores = torch.matmul(Qc, Kc.transpose(-1, -2))
+        inter = torch.matmul(Qc.float(), state.to(q.dtype).float().transpose(-1, -2)) * torch.exp(
+            row_cum).unsqueeze(-1)
+        scores = torch.matmul(Qc.float(), Kc.float().transpose(-1, -2))
         lower = torch.ones(w, w, dtype=torch.bool, device=q.device).tril(-1)
         gap = (cum.unsqueeze(-1) - cum.unsqueeze(-2)).masked_fill(~lower, -torch.inf)
         decay = torch.exp(gap) + torch.diag_embed(diag[:, start:end].transpose(1, 2))
         decay = decay.repeat_interleave(rank, dim=-1).repeat_interleave(rank, dim=-2)
-        y = inter + torch.matmul(scores * decay, Vc) + Dv * Vc
-        y = y.reshape(batch, heads, w, rank, head_dim) * F.silu(rz[:, start:end].permute(0, 2, 1, 3, 4))
+        weighted = (scores * decay).to(act).float()
+        y = inter + torch.matmul(weighted, Vc.float()) + Dv * Vc.float()
+        y = y.reshape(batch, heads, w, rank, head_dim) * F.silu(rz[:, start:end].permute(0, 2, 1, 3, 4).float())
         y = y.sum(dim=3) if mo is None else (y * mo).sum(dim=3)
-        outputs.append(y.transpose(1, 2))
+        outputs.append(y.transpose(1, 2).to(act))
         tail = torch.exp(row_cum[..., -1:] - row_cum).unsqueeze(-1)
-        state = torch.exp(cum[..., -1])[..., None, None] * state + torch.matmul(Vc.transpose(-1, -2), Kc * tail)
-    return torch.cat(outputs, dim=1).to(value.dtype), state
+        state_k = (Kc * tail.to(Kc.dtype)).float()
+        state = torch.exp(cum[..., -1])[..., None, None] * state + torch.matmul(Vc.float().transpose(-1, -2), state_k)
+    return torch.cat(outputs, dim=1), state
 
 
 def _scan_device(q, k, value, gate, adt, dt, trap_logits, D, *, mimo_x, mimo_z, mimo_out, chunk_size,

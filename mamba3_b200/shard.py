@@ -20,6 +20,33 @@ def shard_bounds(batch: int, world: int, rank: int) -> tuple[int, int]:
     return start, start + base + (1 if rank < extra else 0)
 
 
+def all_gather_batch(local: torch.Tensor, batch: int, group=None) -> torch.Tensor:
+    """All-gather the per-rank batch shards ``local`` (this rank's ``shard_bounds`` share of a batch of
+    ``batch``) into the full batch on every rank. Shards are padded to the widest share so one
+    fixed-size NCCL all-gather moves them."""
+    world = dist.get_world_size(group)
+    widest = -(-batch // world)
+    padded = local if local.shape[0] == widest else torch.cat(
+        (local, local.new_zeros((widest - local.shape[0], *local.shape[1:]))))
+    parts = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(parts, padded.contiguous(), group=group)
+    pieces = []
+    for r, part in enumerate(parts):
+        s, e = shard_bounds(batch, world, r)
+        pieces.append(part[: e - s])
+    return torch.cat(pieces, dim=0)
+
+
+def forward_local_gather(model, x_local: torch.Tensor, batch: int, group=None) -> torch.Tensor:
+    """``model`` on this rank's shard ``x_local`` of a batch of ``batch`` sequences, then the all-gather
+    of the outputs: the full ``model(x)`` on every rank, each rank having read only its own inputs."""
+    if x_local.shape[0] > 0:
+        local = model(x_local)
+    else:  # an empty share still joins the gather
+        local = x_local.new_empty((0, *x_local.shape[1:]))
+    return all_gather_batch(local, batch, group)
+
+
 def forward_sharded(model, x: torch.Tensor, group=None) -> torch.Tensor:
     """Run ``model`` on this rank's share of the batch of ``x`` and all-gather the full output.
 
@@ -31,17 +58,7 @@ def forward_sharded(model, x: torch.Tensor, group=None) -> torch.Tensor:
     rank = dist.get_rank(group)
     batch = x.shape[0]
     start, stop = shard_bounds(batch, world, rank)
-    local = model(x[start:stop]) if stop > start else x[:0].new_empty((0, *x.shape[1:]))
-    widest = -(-batch // world)
-    padded = local.new_zeros((widest, *local.shape[1:]))
-    padded[: local.shape[0]] = local
-    parts = [torch.empty_like(padded) for _ in range(world)]
-    dist.all_gather(parts, padded.contiguous(), group=group)
-    pieces = []
-    for r, part in enumerate(parts):
-        s, e = shard_bounds(batch, world, r)
-        pieces.append(part[: e - s])
-    return torch.cat(pieces, dim=0)
+    return forward_local_gather(model, x[start:stop], batch, group)
 
 
 def _gather_heads(local: torch.Tensor, heads: int, world: int, group) -> torch.Tensor:

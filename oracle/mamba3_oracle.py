@@ -308,12 +308,17 @@ def _layer_params(sd: dict, i: int) -> dict:
 
 def _project(cfg: ModelConfig, lp: dict, h: np.ndarray):
     """in_proj split + B/C norm + dt/adt (mamba3/model.py:147-199)."""
-    proj = h @ lp["mixer.in_proj.weight"].T
+    return split_projection(cfg, lp, h @ lp["mixer.in_proj.weight"].T)
+
+
+def split_projection(cfg: ModelConfig, lp: dict, proj: np.ndarray):
+    """Split of an in_proj output [B, L, W] + B/C norm + dt/adt (mamba3/model.py:147-199)."""
+    proj = np.asarray(proj, np.float64)
     di, n, r, nh, s = cfg.d_inner, cfg.d_state, cfg.mimo_rank, cfg.nheads, cfg.num_angles
     sizes = [di, di, n * r, n * r, nh, nh, nh, s]
     offs = np.cumsum([0] + sizes)
     z, x, B, C, dl, al, trap, ang = [proj[..., offs[j]:offs[j + 1]] for j in range(8)]
-    bsz, length = h.shape[:2]
+    bsz, length = proj.shape[:2]
     z = z.reshape(bsz, length, nh, cfg.headdim)
     x = x.reshape(bsz, length, nh, cfg.headdim)
     B = rms_norm(B.reshape(bsz, length, r, n), lp["mixer.B_norm.weight"])
@@ -328,7 +333,13 @@ def _mimo(lp: dict):
 
 
 def _scan_direction(cfg, lp, h, cache, chunked: bool):
-    q, k, x, z, adt, dt, trap, ang = _project(cfg, lp, h)
+    return scan_projection(cfg, lp, h @ lp["mixer.in_proj.weight"].T, cache, chunked)
+
+
+def scan_projection(cfg, lp, proj, cache=None, chunked: bool = True):
+    """One mixer direction from its in_proj output: (y [B,L,H,P] before out_proj, final state,
+    phase [B,L,H,S], rotated biased k [B,L,H,R,N], x [B,L,H,P]) (mamba3/model.py:270-327)."""
+    q, k, x, z, adt, dt, trap, ang = split_projection(cfg, lp, proj)
     phase = phase_scheme(ang, dt, None if cache is None else cache[0])
     q = expand_heads(q, cfg.nheads) + lp["mixer.C_bias"]
     k = expand_heads(k, cfg.nheads) + lp["mixer.B_bias"]

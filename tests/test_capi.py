@@ -79,3 +79,19 @@ def test_binding_refuses_host_tensors():
     with pytest.raises(ValueError, match="CUDA tensors"):
         _ext.step_forward(sizes=dict(batch=1, heads=1, rank=1, d_state=8, head_dim=4, num_angles=2),
                           tensors=dict(value=torch.empty(1)))
+
+
+def test_workspace_query_rejects_non_positive_sizes_without_a_device():
+    """A negative size answers with minus an M3_ERR_* code and a message, and the allocation-free
+    entry point passes that code on instead of a stray status."""
+    lib = _ext.load()
+    lib.m3_scan_fwd_noalloc.argtypes = [ctypes.POINTER(_ext.ScanArgs), ctypes.c_void_p]
+    lib.m3_scan_fwd_noalloc.restype = ctypes.c_int
+    args = _ext.ScanArgs()
+    args.batch, args.length, args.groups, args.heads, args.rank = -3, 100, 1, 8, 1
+    args.d_state, args.head_dim, args.num_angles, args.chunk_hint, args.device = 128, 64, 32, 256, -1
+    assert lib.m3_scan_workspace_bytes(ctypes.byref(args)) == -1  # -M3_ERR_SHAPE
+    assert b"positive" in lib.m3_last_error()
+    args.device = 0
+    rc = lib.m3_scan_fwd_noalloc(ctypes.byref(args), None)
+    assert rc in (1, 5)  # M3_ERR_SHAPE, or M3_ERR_CUDA where no device can be selected

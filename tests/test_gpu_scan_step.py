@@ -206,7 +206,8 @@ def test_step_large_batches_against_oracle(batch, heads):
 def test_step_model_mode_matches_preprocessed_inputs(rank, dtype, two_pass):
     """Raw projection rows + norm weights + dt_bias in the kernel == the same math done first in torch."""
     g = torch.Generator().manual_seed(7 + rank)
-    batch, heads, n, p, s = 5, 6, 128, 64, 32 if rank == 1 else 32
+    # 64 x 6 = 384 (batch, head) pairs reach the two-pass kernels (>= 2 per SM); 5 x 6 the single pass
+    batch, heads, n, p, s = (64 if two_pass else 5), 6, 128, 64, 32
     t = lambda *shape: torch.randn(*shape, generator=g).cuda()
     C, B = t(batch, 1, rank, n).to(dtype) * 3, t(batch, 1, rank, n).to(dtype)
     wq, wk = 1 + 0.1 * t(n), 1 + 0.1 * t(n)
@@ -233,6 +234,10 @@ def test_step_model_mode_matches_preprocessed_inputs(rank, dtype, two_pass):
         y0, c0 = ops._step_device(ex(qn), ex(kn), v, z, adt, dt, tr, ang, D, cache, q_bias=qb, k_bias=kb, **mimo)
         y1, c1 = ops._step_device(ex(C), ex(B), v, z, decay, delta, tr, ang, D, cache, q_bias=qb, k_bias=kb,
                                   q_norm_w=wq, k_norm_w=wk, dt_bias=bias, norm_eps=eps, **mimo)
+    if two_pass:
+        assert _ext.last_step_kernel() == ("two_pass_vec" if rank > 1 and dtype != torch.float32 else "two_pass")
+    else:
+        assert _ext.last_step_kernel() == "single"
     tol = 1e-5 if dtype == torch.float32 else 1e-2
     assert rel_err(y1.float(), y0.float()) < tol
     assert rel_err(c1[1], c0[1]) < tol
