@@ -88,7 +88,8 @@ typedef struct m3_scan_args {
   int32_t chunk_hint;     /* caller's chunk size (validated > 0; the kernel tiles internally) */
   int32_t device;         /* CUDA device ordinal of every tensor and of `stream` (-1: current) */
   float norm_eps;         /* RMS-norm epsilon for q_norm_w / k_norm_w */
-  int32_t reserved;
+  int32_t segments;       /* sequence segments scanned in parallel: 0 = automatic (split only when
+                             batch x heads leaves SMs idle), 1 = never split, n >= 2 = n segments */
   m3_tensor q, k, q_norm_w, k_norm_w, q_bias, k_bias;
   m3_tensor value, gate;
   m3_tensor adt, dt, trap, dt_bias;
@@ -160,6 +161,10 @@ int m3_scan_fwd(const m3_scan_args* args, void* stream);
 /* Bytes of float32 workspace m3_scan_fwd needs for these arguments (0 = none); a negative value
  * is minus an M3_ERR_* code (null arguments, non-positive sizes) with m3_last_error() set. */
 int64_t m3_scan_workspace_bytes(const m3_scan_args* args);
+
+/* Number of sequence segments the tensor-core scan kernel splits these sizes into (args->segments
+ * and the GPU's SM count decide; 1 = no split). Negative: minus an M3_ERR_* code. */
+int m3_scan_segments(const m3_scan_args* args);
 
 /* Fixed scratch size of m3_scan_fwd_noalloc, per GPU that loads the library: 8 MiB. */
 #define M3_NOALLOC_WORKSPACE_BYTES (8 * 1024 * 1024)

@@ -8,6 +8,7 @@ unloadable library raises ``RuntimeError`` when a CUDA call needs it.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -54,7 +55,7 @@ class ScanArgs(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in (
         "batch", "length", "groups", "heads", "rank", "d_state", "head_dim", "num_angles",
         "reverse", "mimo_rotation", "chunk_hint", "device")] + [
-        ("norm_eps", ctypes.c_float), ("reserved", ctypes.c_int32)] + [
+        ("norm_eps", ctypes.c_float), ("segments", ctypes.c_int32)] + [
         (name, M3Tensor) for name in _SCAN_TENSORS]
 
 
@@ -109,6 +110,8 @@ def load() -> ctypes.CDLL:
         lib.m3_residual_rmsnorm.restype = ctypes.c_int
         lib.m3_last_scan_kernel.argtypes = []
         lib.m3_last_scan_kernel.restype = ctypes.c_char_p
+        lib.m3_scan_segments.argtypes = [ctypes.POINTER(ScanArgs)]
+        lib.m3_scan_segments.restype = ctypes.c_int
         lib.m3_last_step_kernel.argtypes = []
         lib.m3_last_step_kernel.restype = ctypes.c_char_p
         if lib.m3_abi_version() != ABI_VERSION:
@@ -149,12 +152,23 @@ def _check(rc: int, lib) -> None:
         raise RuntimeError(f"mamba3_b200 kernel error {rc}: {msg}")
 
 
+def _segments(segments: int | None) -> int:
+    if segments is None:
+        segments = int(os.environ.get("MAMBA3_B200_SEGMENTS", "0") or 0)
+    if segments < 0:
+        raise ValueError("segments must be >= 0")
+    return int(segments)
+
+
 @torch.compiler.disable
 def scan_forward(*, sizes: dict, tensors: dict, reverse: bool = False, mimo_rotation: bool = False,
-                 chunk_hint: int = 64, norm_eps: float = 1e-5) -> None:
-    """Enqueue ``m3_scan_fwd`` on the current stream of the tensors' device."""
+                 chunk_hint: int = 64, norm_eps: float = 1e-5, segments: int | None = None) -> None:
+    """Enqueue ``m3_scan_fwd`` on the current stream of the tensors' device. ``segments``: 0 / None =
+    automatic sequence split, 1 = never split, n >= 2 = n segments (``MAMBA3_B200_SEGMENTS`` sets
+    the default)."""
     lib = load()
     args = ScanArgs()
+    args.segments = _segments(segments)
     for key, val in sizes.items():
         setattr(args, key, int(val))
     args.reverse = int(reverse)
@@ -233,7 +247,7 @@ def device_error(clear: bool = True) -> int:
 
 @torch.compiler.disable
 def scan_forward_noalloc(*, sizes: dict, tensors: dict, reverse: bool = False, mimo_rotation: bool = False,
-                         chunk_hint: int = 64, norm_eps: float = 1e-5) -> None:
+                         chunk_hint: int = 64, norm_eps: float = 1e-5, segments: int | None = None) -> None:
     """Enqueue ``m3_scan_fwd_noalloc``: the scan with the library's fixed scratch array instead of a
     caller workspace, for hosts that cannot allocate device memory at the call site (see the
     header). Nothing is allocated here either."""
@@ -241,6 +255,7 @@ def scan_forward_noalloc(*, sizes: dict, tensors: dict, reverse: bool = False, m
     lib.m3_scan_fwd_noalloc.argtypes = [ctypes.POINTER(ScanArgs), ctypes.c_void_p]
     lib.m3_scan_fwd_noalloc.restype = ctypes.c_int
     args = ScanArgs()
+    args.segments = _segments(segments)
     for key, val in sizes.items():
         setattr(args, key, int(val))
     args.reverse = int(reverse)

@@ -15,6 +15,7 @@ cudaError_t launch_scan_simt(const m3_scan_args& a, cudaStream_t stream);
 size_t scan_simt_smem_bytes(int rank, int N, int P, int S);
 bool scan_umma_supported(const m3_scan_args& a);
 int64_t scan_umma_workspace_bytes(const m3_scan_args& a);
+int scan_umma_segments(const m3_scan_args& a);
 cudaError_t launch_scan_umma(const m3_scan_args& a, cudaStream_t stream);
 }  // namespace m3
 
@@ -143,6 +144,13 @@ int64_t m3_scan_workspace_bytes(const m3_scan_args* args) {
   if (a.batch <= 0 || a.length <= 0 || a.heads <= 0 || a.groups <= 0 || a.rank <= 0 || a.num_angles < 0)
     return -fail(M3_ERR_SHAPE, "batch, length, heads, groups and rank must be positive");
   return m3::scan_umma_supported(a) ? m3::scan_umma_workspace_bytes(a) : 0;
+}
+
+int m3_scan_segments(const m3_scan_args* args) {
+  if (args == nullptr) return -fail(M3_ERR_ARGUMENT, "null argument struct");
+  if (args->batch <= 0 || args->length <= 0 || args->heads <= 0)
+    return -fail(M3_ERR_SHAPE, "batch, length and heads must be positive");
+  return m3::scan_umma_segments(*args);
 }
 
 int m3_scan_fwd(const m3_scan_args* args, void* stream) {

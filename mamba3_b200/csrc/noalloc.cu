@@ -42,6 +42,8 @@ float* scratch_for(int device) {
 
 namespace m3 {
 int report_error(int code, const char* msg);
+bool scan_umma_supported(const m3_scan_args& a);
+int scan_umma_segments(const m3_scan_args& a);
 }
 
 extern "C" int m3_scan_fwd_noalloc(const m3_scan_args* args, void* stream) {
@@ -56,8 +58,16 @@ extern "C" int m3_scan_fwd_noalloc(const m3_scan_args* args, void* stream) {
     return m3::report_error(M3_ERR_CUDA, "m3_scan_fwd_noalloc: cannot query the current device");
   }
   a.workspace = m3_tensor{};
-  const int64_t need = m3_scan_workspace_bytes(&a);
+  int64_t need = m3_scan_workspace_bytes(&a);
   if (need < 0) return (int)(-need);
+  // A sequence split into segments keeps per-segment records in the scratch too; when they do not
+  // fit, scan in fewer segments (the results then agree with m3_scan_fwd within rounding).
+  if (need > kNoAllocWorkspaceBytes && m3::scan_umma_supported(a)) {
+    for (int n = m3::scan_umma_segments(a) - 1; n >= 1 && need > kNoAllocWorkspaceBytes; --n) {
+      a.segments = n;
+      need = m3_scan_workspace_bytes(&a);
+    }
+  }
   if (need > kNoAllocWorkspaceBytes) {
     const std::string msg = "m3_scan_fwd_noalloc: these sizes need " + std::to_string(need) +
                             " bytes of scratch, above the fixed limit of " +

@@ -32,6 +32,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstring>
 #include <initializer_list>
 #include <mutex>
@@ -384,12 +385,34 @@ __global__ void __launch_bounds__(256) token_prep_kernel(const m3_scan_args a, f
   }
 }
 
+// Sequence segments. A long sequence with few (batch, head) pairs is split into segments of
+// seg_len tokens (a multiple of 64, so the 64-token phase blocks line up), each scanned by its own
+// CTA as a continuation of the previous one (the exact prefill -> continue semantics: the segment
+// end acts as a sequence end, and the next segment folds the endpoint term of the boundary token
+// through its initial k / value). Three launches: the state pass (kStateOnly) runs every segment but
+// the last from a zero state and zero phase and records its end state, last phase, last rotated k,
+// total decay and first-token endpoint weight; seg_combine_kernel scans those records over the
+// segments in FP32 (rotating each local state and k by the true starting phase) into each
+// segment's initial cache; the main pass then runs every segment from its initial cache.
+// Per (segment, batch, head) record of floats: state [P][N], phase [32], k [R][N], c0, total decay.
+__host__ __device__ constexpr int seg_rec(int R) { return kP * kN + kMaxAngles + R * kN + 4; }
+constexpr int kRecPhase = kP * kN, kRecK = kP * kN + kMaxAngles;
+__host__ __device__ constexpr int rec_c0(int R) { return kRecK + R * kN; }
+struct SegArgs {
+  int seg_len;   // tokens per segment (the whole sequence when nseg == 1)
+  int nseg;
+  int nblk;      // 64-token phase blocks per segment (seg_len / 64)
+  float* part;   // state-pass records [nseg][B][H][seg_rec(R)]
+  float* init;   // initial caches of the main pass [nseg][B][H][seg_rec(R)] (slot 0 unused)
+  float* blk;    // state pass: in-block phase totals [nseg][B][H][nblk][32]
+};
+
 // x - 2pi * trunc(x / 2pi): the remainder of fmod (exact for |x| < 2pi, a few ulp beyond).
 __device__ __forceinline__ float fmod_2pi(float x) { return x - kTwoPi * truncf(x * (1.0f / kTwoPi)); }
 
-template <typename T, int R>
+template <typename T, int R, bool kStateOnly>
 __global__ void __launch_bounds__(kThreads, 2)
-    scan_umma_kernel(const m3_scan_args a, const __grid_constant__ TileMaps tm, int vec_y) {
+    scan_umma_kernel(const m3_scan_args a, const __grid_constant__ TileMaps tm, int vec_y, const SegArgs sg) {
   using Lay = Layout<R>;
   constexpr int TOK = Lay::TOK;
   constexpr int kRowsPerWarp = kRows / kWarps;               // staging rows per warp (8)
@@ -397,8 +420,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   // Largest |cum - cmid| for which the decay can be split into per-row operand factors
   // e^{cum_i - cmid} (Q rows) and e^{cmid - cum_j} (K rows) without leaving the 16-bit range.
   constexpr float kLim = kBf16 ? 80.0f : 8.0f;
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int S = a.num_angles, L = a.length;
+  const int h = blockIdx.x, b = blockIdx.y, seg = blockIdx.z;
+  // This CTA's segment [seg_begin, L) in scan order; its end acts as the sequence end.
+  const int seg_begin = seg * sg.seg_len;
+  const int L = min(a.length, seg_begin + sg.seg_len);
+  const bool last_seg = L == a.length;
+  const int S = a.num_angles;
   const int g = h / (a.heads / a.groups);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int quad = warp & 3, part = warp >> 2;  // TMEM lane quadrant, column half
@@ -435,7 +462,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_addr = smem_u32(bar);
   const uint32_t sbase = smem_u32(smem);
   const bool has_phase = a.phase.data != nullptr || a.angles.data != nullptr;
-  const bool has_ws = a.workspace.data != nullptr;
+  // per-token workspace rows (RMS factors, pi tanh(angle)) exist exactly when the pre-pass runs
+  const bool has_ws = a.q_norm_w.data != nullptr || a.angles.data != nullptr;
   const float* ws = static_cast<const float*>(a.workspace.data);
 
   const T* qp = static_cast<const T*>(a.q.data);
@@ -449,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int64_t k_b0 = b * a.k.stride[0] + g * a.k.stride[2];
   const int64_t v_b0 = b * a.value.stride[0] + h * a.value.stride[2];
   const int64_t z_b0 = b * a.gate.stride[0] + h * a.gate.stride[2];
-  const int64_t ws_b = (int64_t)b * L * WS;
+  const int64_t ws_b = (int64_t)b * a.length * WS;
 
   // ---- loads of a tile, issued one tile ahead (cp.async for rows; see the tile loop) ----
   // q/k rows go straight into the Q'/K' tiles (processed in place), raw x into the W tile, z into the
@@ -457,9 +485,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto issue_qk = [&](int t0n, int ntn) {
     if (use_tma) {
       if (tid == 0) {
-        mbar_expect_tx(tma_bar, 4u * (kRows * 64 * 2));
-        tma_load5(sbase + kOffQ, &tm.q, 0, 0, g, t0n, b, tma_bar);
-        tma_load5(sbase + kOffQ + kRows * 128, &tm.q, 64, 0, g, t0n, b, tma_bar);
+        mbar_expect_tx(tma_bar, (kStateOnly ? 2u : 4u) * (kRows * 64 * 2));
+        if (!kStateOnly) {  // the state pass needs only the k rows
+          tma_load5(sbase + kOffQ, &tm.q, 0, 0, g, t0n, b, tma_bar);
+          tma_load5(sbase + kOffQ + kRows * 128, &tm.q, 64, 0, g, t0n, b, tma_bar);
+        }
         tma_load5(sbase + kOffK, &tm.k, 0, 0, g, t0n, b, tma_bar);
         tma_load5(sbase + kOffK + kRows * 128, &tm.k, 64, 0, g, t0n, b, tma_bar);
       }
@@ -472,7 +502,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (j < ntn) {
         const int t = scan_token(a, t0n + j);
         const uint32_t off = swz(row, c8 * 8, kRows);
-        cp_async16(sbase + kOffQ + off, qp + q_b0 + (int64_t)t * a.q.stride[1] + r * a.q.stride[3] + c8 * 8);
+        if (!kStateOnly)
+          cp_async16(sbase + kOffQ + off, qp + q_b0 + (int64_t)t * a.q.stride[1] + r * a.q.stride[3] + c8 * 8);
         cp_async16(sbase + kOffK + off, kp + k_b0 + (int64_t)t * a.k.stride[1] + r * a.k.stride[3] + c8 * 8);
       }
     }
@@ -497,13 +528,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto issue_z = [&](int t0n, int ntn, int par) {
     const uint32_t zoff = kOffZ + par * (kRows * kP * 2);
     if (use_tma) {  // the z rows and (with a workspace) the workspace rows of the tile
-      if (tid == 0) {
-        mbar_expect_tx(tma_bar, (uint32_t)(TOK * kP * 2) + (has_ws ? (uint32_t)(TOK * WS * 4) : 0u));
-        tma_load4(sbase + zoff, &tm.z, 0, h, t0n, b, tma_bar);
+      if (tid == 0) {  // (the state pass needs no z rows)
+        mbar_expect_tx(tma_bar, (kStateOnly ? 0u : (uint32_t)(TOK * kP * 2)) + (has_ws ? (uint32_t)(TOK * WS * 4) : 0u));
+        if (!kStateOnly) tma_load4(sbase + zoff, &tm.z, 0, h, t0n, b, tma_bar);
         if (has_ws) tma_load3(smem_u32(wsb), &tm.ws, 0, t0n, b, tma_bar);
       }
       return;
     }
+    if (kStateOnly) return;
     for (int c = tid; c < TOK * (kP / 8); c += kThreads) {
       const int j = c >> 3, c8 = c & 7;
       if (j < ntn) {
@@ -650,14 +682,32 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   const bool has_norm = a.q_norm_w.data != nullptr;
   const bool has_bias = a.q_bias.data != nullptr;
+  // Initial cache of this segment: the caller's for the first segment; for later segments of the
+  // main pass the combined records (state, last phase, rotated k of the token before the segment)
+  // and that token's value row; nothing (zero state, zero phase) for later segments of the state pass.
+  m3_tensor ist = a.initial_state, ikt = a.initial_k, ivt = a.initial_value, iph = a.initial_phase;
+  if (seg > 0) {
+    ist = ikt = ivt = iph = m3_tensor{};
+    if (!kStateOnly) {
+      constexpr int REC = seg_rec(R);
+      float* rec = sg.init + (int64_t)seg * a.batch * a.heads * REC;
+      const int64_t sb = (int64_t)a.heads * REC;
+      ist = m3_tensor{rec, M3_F32, 4, {sb, REC, kN, 1, 0, 0}};
+      iph = m3_tensor{rec + kRecPhase, M3_F32, 3, {sb, REC, 1, 0, 0, 0}};
+      ikt = m3_tensor{rec + kRecK, M3_F32, 4, {sb, REC, kN, 1, 0, 0}};
+      const int tprev = scan_token(a, seg_begin - 1);
+      ivt = m3_tensor{const_cast<T*>(vp) + (int64_t)tprev * a.value.stride[1], a.value.dtype, 3,
+                      {a.value.stride[0], a.value.stride[2], a.value.stride[3], 0, 0, 0}};
+    }
+  }
   // Loads of the first tile.
   {
-    const int nt0 = min(TOK, L);
-    issue_qk(0, nt0);
-    issue_x(0, nt0);
-    issue_z(0, nt0, 0);
-    fetch_small(0, nt0);
-    fetch_scalars(0, nt0);
+    const int nt0 = min(TOK, L - seg_begin);
+    issue_qk(seg_begin, nt0);
+    issue_x(seg_begin, nt0);
+    issue_z(seg_begin, nt0, 0);
+    fetch_small(seg_begin, nt0);
+    fetch_scalars(seg_begin, nt0);
     finish_scalars();
     cp_async_commit();
   }
@@ -670,11 +720,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---- initial state into TMEM: S^T[n][p] = S0[p][n] + c0 sum_r (v mx_r)[p] k_r[n] ----
   {
     float c0 = 0.0f;
-    if (a.initial_k.data) {
+    if (ikt.data || (kStateOnly && seg > 0)) {
       float dt0, adt0;
-      const int t_first = scan_token(a, 0);
+      const int t_first = scan_token(a, seg_begin);
       load_dt_adt(a, b, t_first, h, dt0, adt0);
       c0 = dt0 * (1.0f - sigmoidf_(load_trap(a, b, t_first, h)));
+      // the state pass records the endpoint weight of its first token for the combine
+      if (kStateOnly && tid == 0)
+        sg.part[((int64_t)(seg * a.batch + b) * a.heads + h) * seg_rec(R) + rec_c0(R)] = c0;
     }
     const int n = quad * 32 + lane;
     uint32_t r32[32];
@@ -682,13 +735,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int j = 0; j < 32; ++j) {
       const int p = part * 32 + j;
       float s = 0.0f;
-      if (a.initial_state.data) {
-        const m3_tensor& t = a.initial_state;
+      if (ist.data) {
+        const m3_tensor& t = ist;
         s = ld_t(t, b * t.stride[0] + h * t.stride[1] + p * t.stride[2] + n * t.stride[3]);
       }
-      if (a.initial_k.data) {
-        const m3_tensor& ik = a.initial_k;
-        const m3_tensor& iv = a.initial_value;
+      if (ikt.data) {
+        const m3_tensor& ik = ikt;
+        const m3_tensor& iv = ivt;
         const float v = ld_t(iv, b * iv.stride[0] + h * iv.stride[1] + p * iv.stride[2]);
         float acc = 0.0f;
 #pragma unroll
@@ -727,15 +780,17 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
   for (int k = 0; k < kPhA; ++k) {
     const int sidx = ph_s0 + k;
-    ph_off[k] = (a.initial_phase.data && sidx < S)
-                    ? ld_t(a.initial_phase, b * a.initial_phase.stride[0] + h * a.initial_phase.stride[1] +
-                                                sidx * a.initial_phase.stride[2])
+    ph_off[k] = (iph.data && sidx < S)
+                    ? ld_t(iph, b * iph.stride[0] + h * iph.stride[1] + sidx * iph.stride[2])
                     : 0.0f;
     ph_loc[k] = 0.0f;
   }
   uint32_t tma_phase = 0;
   int tile = 0;
-  for (int t0 = 0; t0 < L; t0 += TOK, ++tile) {
+  float decay_sum = 0.0f;  // state pass: total log-decay of the segment
+  // the state pass's record of this (segment, batch, head)
+  float* const prec = kStateOnly ? sg.part + ((int64_t)(seg * a.batch + b) * a.heads + h) * seg_rec(R) : nullptr;
+  for (int t0 = seg_begin; t0 < L; t0 += TOK, ++tile) {
     const int nt = min(TOK, L - t0);
     const int t0n = t0 + TOK, ntn = min(TOK, L - t0n);  // next tile (ntn <= 0: none)
     M3_MARK(0);
@@ -860,6 +915,15 @@ __global__ void __launch_bounds__(kThreads, 2)
             ph[1][k] = fmod_2pi((ph_loc[k] + x) + ph_off[k]);
             ph_loc[k] += tot;
           }
+          // The state pass records every completed 64-token block's in-block phase total, so the
+          // combine can replay the exact block-offset carry (fmod at every block end) across it.
+          if (kStateOnly && ((t0 + TOK) % kPhaseBlock) == 0 && lane == 0) {
+            float* bp = sg.blk + (((int64_t)(seg * a.batch + b) * a.heads + h) * sg.nblk +
+                                  (t0 + TOK - seg_begin) / kPhaseBlock - 1) * kMaxAngles;
+#pragma unroll
+            for (int k = 0; k < kPhA; ++k)
+              if (s0 + k < S) bp[s0 + k] = ph_loc[k];
+          }
         } else {
 #pragma unroll
           for (int m = 0; m < 2; ++m) {
@@ -883,7 +947,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             float cs[kPhA], sn[kPhA];
 #pragma unroll
             for (int k = 0; k < kPhA; ++k) __sincosf(ph[m][k], &sn[k], &cs[k]);  // |phase| < 2 pi
-            if (t0 + j == L - 1 && a.final_phase.data) {
+            if (!kStateOnly && t0 + j == L - 1 && last_seg && a.final_phase.data) {
               const m3_tensor& fp = a.final_phase;
 #pragma unroll
               for (int k = 0; k < kPhA; ++k)
@@ -921,6 +985,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncthreads();
     const bool fact = mode[2] != 0.0f;
+    if (kStateOnly) decay_sum += mode[1];
     M3_MARK(3);
 
     // ---- stage Q', K' in place (packed 16-bit math): q' = rot(q rq w + b) fq, k' = rot(k rk w + b) fk.
@@ -939,8 +1004,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t off0 = qko + swz(row, 8 * c, kRows), off1 = qko + swz(row, 64 + 8 * c, kRows);
       uint32_t qv[8], kv[8];
       {
-        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + off0);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(smem + off1);
+        // (the state pass loads no q rows: its Q' words are never stored, so their math folds away)
+        const uint4 q0 = kStateOnly ? make_uint4(0, 0, 0, 0) : *reinterpret_cast<const uint4*>(smem + off0);
+        const uint4 q1 = kStateOnly ? make_uint4(0, 0, 0, 0) : *reinterpret_cast<const uint4*>(smem + off1);
         const uint4 k0 = *reinterpret_cast<const uint4*>(smem + off0 + kRows * kN * 2);
         const uint4 k1 = *reinterpret_cast<const uint4*>(smem + off1 + kRows * kN * 2);
         qv[0] = q0.x; qv[1] = q0.y; qv[2] = q0.z; qv[3] = q0.w;
@@ -1007,7 +1073,15 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
       }
-      if (valid && a.final_k.data && t0 + j == L - 1) {
+      if (kStateOnly && valid && t0 + j == L - 1) {
+        float* fkp = prec + kRecK + r * kN;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int n = (e < 4 ? 8 * c : 64 + 8 * c) + 2 * (e & 3);
+          fkp[n] = lo16<T>(kv[e]);
+          fkp[n + 1] = hi16<T>(kv[e]);
+        }
+      } else if (valid && last_seg && a.final_k.data && t0 + j == L - 1) {
         const m3_tensor& fkt = a.final_k;
         T* fkp = static_cast<T*>(fkt.data) + b * fkt.stride[0] + h * fkt.stride[1] + r * fkt.stride[2];
 #pragma unroll
@@ -1019,10 +1093,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       // Rows outside the sequence (zero-filled by the TMA) would still carry the bias: zero them.
       const uint32_t fq2 = valid ? bcast2<T>(fq[j]) : 0u, fk2 = valid ? bcast2<T>(fk[j]) : 0u;
-      *reinterpret_cast<uint4*>(smem + off0) =
-          make_uint4(mul2<T>(qv[0], fq2), mul2<T>(qv[1], fq2), mul2<T>(qv[2], fq2), mul2<T>(qv[3], fq2));
-      *reinterpret_cast<uint4*>(smem + off1) =
-          make_uint4(mul2<T>(qv[4], fq2), mul2<T>(qv[5], fq2), mul2<T>(qv[6], fq2), mul2<T>(qv[7], fq2));
+      if (!kStateOnly) {
+        *reinterpret_cast<uint4*>(smem + off0) =
+            make_uint4(mul2<T>(qv[0], fq2), mul2<T>(qv[1], fq2), mul2<T>(qv[2], fq2), mul2<T>(qv[3], fq2));
+        *reinterpret_cast<uint4*>(smem + off1) =
+            make_uint4(mul2<T>(qv[4], fq2), mul2<T>(qv[5], fq2), mul2<T>(qv[6], fq2), mul2<T>(qv[7], fq2));
+      }
       *reinterpret_cast<uint4*>(smem + off0 + kRows * kN * 2) =
           make_uint4(mul2<T>(kv[0], fk2), mul2<T>(kv[1], fk2), mul2<T>(kv[2], fk2), mul2<T>(kv[3], fk2));
       *reinterpret_cast<uint4*>(smem + off1 + kRows * kN * 2) =
@@ -1068,6 +1144,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int n = quad * 32 + lane;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        if (kStateOnly) break;  // the state pass has no inter-tile output term
         uint32_t w[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -1089,18 +1166,20 @@ __global__ void __launch_bounds__(kThreads, 2)
     // they land), then inter = Q' St and X += K'^T V (or V2), which finish behind the W section ----
     if (tid == 0) {
       fence_after();
+      if (!kStateOnly) {
 #pragma unroll
-      for (int kk = 0; kk < kN / 16; ++kk) {
-        const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-        mma_f16(tmem + kColScores, sdesc(sbase + kOffQ + koff, 16, 1024), sdesc(sbase + kOffK + koff, 16, 1024),
-                id_scores, kk > 0);
-      }
-      mma_commit(bar_addr);
+        for (int kk = 0; kk < kN / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+          mma_f16(tmem + kColScores, sdesc(sbase + kOffQ + koff, 16, 1024), sdesc(sbase + kOffK + koff, 16, 1024),
+                  id_scores, kk > 0);
+        }
+        mma_commit(bar_addr);
 #pragma unroll
-      for (int kk = 0; kk < kN / 16; ++kk) {
-        const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-        mma_f16(tmem + kColInter, sdesc(sbase + kOffQ + koff, 16, 1024),
-                sdesc(sbase + kOffST + kk * 2048, kN * 128, 1024), id_nmn, kk > 0);
+        for (int kk = 0; kk < kN / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+          mma_f16(tmem + kColInter, sdesc(sbase + kOffQ + koff, 16, 1024),
+                  sdesc(sbase + kOffST + kk * 2048, kN * 128, 1024), id_nmn, kk > 0);
+        }
       }
       const uint32_t vsrc = fact ? kOffV : kOffV2;
 #pragma unroll
@@ -1115,6 +1194,24 @@ __global__ void __launch_bounds__(kThreads, 2)
       fetch_scalars(t0n, ntn);
       fetch_small(t0n, ntn);
       issue_z(t0n, ntn, (tile + 1) & 1);
+    }
+    if constexpr (kStateOnly) {
+      // The state update is the state pass's only MMA; once it has read K' and V the next tile's rows
+      // can land.
+      if (tid == 0 && !mbar_wait(bar_b, phase_bit)) *abort_flag = 1;
+      phase_bit ^= 1;
+      __syncthreads();
+      fence_after();
+      if (ntn > 0) {
+        issue_qk(t0n, ntn);
+        issue_x(t0n, ntn);
+      }
+      cp_async_commit();
+      if (ntn > 0) finish_scalars();
+      fence_before();
+      __syncthreads();
+      if (*abort_flag) break;
+      continue;
     }
     // One thread polls the barrier; the others wait at __syncthreads without taking issue slots.
     if (tid == 0 && !mbar_wait(bar_addr, phase_bit)) *abort_flag = 1;
@@ -1313,21 +1410,154 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   // ---- final state: S[p][n] = phi X^T ----
   fence_after();
-  if (!*abort_flag) {
+  if (!*abort_flag && (kStateOnly || last_seg)) {
     uint32_t r32[32];
     M3_TMEM_LD32(tmem + lane_base + kColState + part * 32, r32);
     tmem_wait_ld();
     const int n = quad * 32 + lane;
-    const m3_tensor& fs = a.final_state;
-    float* fsp = static_cast<float*>(fs.data) + b * fs.stride[0] + h * fs.stride[1] + n * fs.stride[3];
+    if (kStateOnly) {  // the segment's record: end state [P][N] and total log-decay
 #pragma unroll
-    for (int j = 0; j < 32; ++j) fsp[(part * 32 + j) * fs.stride[2]] = __uint_as_float(r32[j]) * phi;
+      for (int j = 0; j < 32; ++j) prec[(part * 32 + j) * kN + n] = __uint_as_float(r32[j]) * phi;
+      if (tid == 0) prec[rec_c0(R) + 1] = decay_sum;
+    } else {
+      const m3_tensor& fs = a.final_state;
+      float* fsp = static_cast<float*>(fs.data) + b * fs.stride[0] + h * fs.stride[1] + n * fs.stride[3];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) fsp[(part * 32 + j) * fs.stride[2]] = __uint_as_float(r32[j]) * phi;
+    }
   }
   fence_before();
   __syncthreads();
   if (warp == 0) {
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// Scan over segments (one CTA per (head, batch), FP32): turns the state-pass records into the
+// initial cache of every later segment. phi_s, the block offset at the start of segment s, follows
+// from phi_{s-1} by replaying the blocked carry over segment s - 1's recorded block totals T_k,
+// phi <- fmod(phi + T_k, 2 pi) (model.py:246-251, bit for bit what an unsplit scan carries). With the
+// true end state S and last rotated k of segment s - 1, and segment s's record (local end state S_s,
+// local last rotated k_s, endpoint weight c0_s of its first token, total log-decay D_s):
+//   S <- e^{D_s} (S + c0_s sum_r (v mx_r) k_r^T) + S_s R(phi_s)^T     (v: value of the token before s)
+//   k <- R(phi_s) k_s
+// R(phi) rotates the rotation pairs of the N axis (SISO (2i, 2i+1), MIMO (i, 2S + i)): the state pass
+// ran segment s from phase 0, and rotating every k of a segment by one extra angle rotates its whole
+// state contribution by it (mamba3/ops.py:35-84 pair layout, ops.py:804-816 state carry). A
+// precomputed phase tensor already holds absolute phases: then nothing is rotated.
+// Thread t owns state row p = t / 4 and the columns [16 q, 16 q + 16) and [64 + 16 q, 64 + 16 q + 16),
+// q = t % 4, so both members of every rotation pair stay in one thread.
+template <int R>
+__global__ void __launch_bounds__(256) seg_combine_kernel(const m3_scan_args a, const SegArgs sg) {
+  constexpr int REC = seg_rec(R);
+  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int S = a.num_angles;
+  const bool mimo = a.mimo_rotation != 0;
+  const bool carry = a.angles.data != nullptr;  // in-kernel phase: segments ran from phase 0
+  const int p = tid >> 2, q = tid & 3;
+  __shared__ float ph[kMaxAngles], cs[kMaxAngles], sn[kMaxAngles];
+  __shared__ float kt[R * kN];
+  __shared__ float xv[R * kP];
+  auto rec = [&](float* base, int s_) { return base + ((int64_t)(s_ * a.batch + b) * a.heads + h) * REC; };
+  auto col = [&](int i) { return i < 16 ? 16 * q + i : 64 + 16 * q + (i - 16); };
+  float st[32];
+  {
+    const float* r0 = rec(sg.part, 0);
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(r0 + p * kN + col(i));
+      st[i] = v.x, st[i + 1] = v.y, st[i + 2] = v.z, st[i + 3] = v.w;
+    }
+    if (tid < kMaxAngles) {
+      const m3_tensor& ip = a.initial_phase;
+      ph[tid] = (carry && ip.data && tid < S) ? ld_t(ip, b * ip.stride[0] + h * ip.stride[1] + tid * ip.stride[2]) : 0.0f;
+    }
+    for (int i = tid; i < R * kN; i += blockDim.x) kt[i] = r0[kRecK + i];
+  }
+  __syncthreads();
+  for (int s_ = 1; s_ < sg.nseg; ++s_) {
+    float* ri = rec(sg.init, s_);
+    if (carry && tid < S) {  // block offset at the start of segment s_
+      const float* bt = sg.blk + ((int64_t)((s_ - 1) * a.batch + b) * a.heads + h) * sg.nblk * kMaxAngles + tid;
+      float off = ph[tid];
+      for (int k = 0; k < sg.nblk; ++k) off = fmodf(off + bt[k * kMaxAngles], kTwoPi);
+      ph[tid] = off;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 32; i += 4)
+      *reinterpret_cast<float4*>(ri + p * kN + col(i)) = make_float4(st[i], st[i + 1], st[i + 2], st[i + 3]);
+    if (tid < kMaxAngles) ri[kRecPhase + tid] = ph[tid];
+    for (int i = tid; i < R * kN; i += blockDim.x) ri[kRecK + i] = kt[i];
+    if (s_ == sg.nseg - 1) break;
+    const float* rp = rec(sg.part, s_);
+    const float c0 = rp[rec_c0(R)], decay = __expf(rp[rec_c0(R) + 1]);
+    const int tprev = scan_token(a, s_ * sg.seg_len - 1);
+    if (tid < kP) {
+      const float v = ld_t(a.value, b * a.value.stride[0] + (int64_t)tprev * a.value.stride[1] + h * a.value.stride[2] +
+                                        tid * a.value.stride[3]);
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        xv[r * kP + tid] = R > 1 ? v * ld_t(a.mimo_x, h * a.mimo_x.stride[0] + r * a.mimo_x.stride[1] +
+                                                           tid * a.mimo_x.stride[2])
+                                 : v;
+    }
+    if (tid < kMaxAngles) sincosf(carry && tid < S ? ph[tid] : 0.0f, &sn[tid], &cs[tid]);
+    __syncthreads();
+    float loc[32];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(rp + p * kN + col(i));
+      loc[i] = v.x, loc[i + 1] = v.y, loc[i + 2] = v.z, loc[i + 3] = v.w;
+    }
+    if (!carry) {
+      // absolute phases: the local records are already true
+    } else if (!mimo) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        const int ang = (16 * q + i) >> 1;
+        if (ang < S) {
+          const float x0 = loc[i], x1 = loc[i + 1];
+          loc[i] = x0 * cs[ang] - x1 * sn[ang];
+          loc[i + 1] = x0 * sn[ang] + x1 * cs[ang];
+        }
+      }
+    } else if (16 * q < S) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int ang = 16 * q + i;
+        if (ang < S) {
+          const float x0 = loc[i], x1 = loc[16 + i];
+          loc[i] = x0 * cs[ang] - x1 * sn[ang];
+          loc[16 + i] = x0 * sn[ang] + x1 * cs[ang];
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int n = col(i);
+      float u = 0.0f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) u += xv[r * kP + p] * kt[r * kN + n];
+      st[i] = decay * (st[i] + c0 * u) + loc[i];
+    }
+    __syncthreads();  // every thread has read kt and xv
+    // k of the segment's last token: its local rotation composed with the starting phase.
+    for (int t = tid; t < R * 64; t += blockDim.x) {
+      const int r = t >> 6, i = t & 63;
+      const int n0 = mimo ? i : 2 * i, n1 = mimo ? i + 64 : 2 * i + 1;
+      const float x0 = rp[kRecK + r * kN + n0], x1 = rp[kRecK + r * kN + n1];
+      const int ang = i;
+      if (carry && ang < S) {
+        kt[r * kN + n0] = x0 * cs[ang] - x1 * sn[ang];
+        kt[r * kN + n1] = x0 * sn[ang] + x1 * cs[ang];
+      } else {
+        kt[r * kN + n0] = x0;
+        kt[r * kN + n1] = x1;
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -1367,13 +1597,80 @@ static bool encode_rows(CUtensorMap* map, const m3_tensor& t, int rank, const ui
          CUDA_SUCCESS;
 }
 
+// Segment plan of a call: how many segments and how long. Automatic (a.segments == 0): one segment
+// while the (batch, head) pairs fill every SM; otherwise as many segments as fill the two CTA slots
+// of every SM, each at least kMinSegTokens long. a.segments == 1 forces one segment, n >= 2 asks for
+// n (at least 64 tokens each). Segments hold a multiple of 64 tokens (the phase block).
+constexpr int kMinSegTokens = 256;
+
+static int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();  // clear the sticky-free error of the query
+      return 148;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+struct SegPlan {
+  int nseg, seg_len;
+};
+
+static SegPlan seg_plan(const m3_scan_args& a) {
+  const int64_t L = a.length;
+  int want = 1;
+  if (a.segments >= 2) {
+    want = (int)std::min<int64_t>(a.segments, (L + 63) / 64);
+  } else if (a.segments == 0) {
+    const int64_t pairs = (int64_t)a.batch * a.heads;
+    const int sms = sm_count();
+    if (pairs < sms) want = (int)std::min<int64_t>(2LL * sms / pairs, L / kMinSegTokens);
+  }
+  want = std::max(1, std::min(want, 64));
+  if (want == 1) return {1, (int)L};
+  const int64_t len = ((L + want - 1) / want + 63) / 64 * 64;
+  return {(int)((L + len - 1) / len), (int)len};
+}
+
+// Floats of the per-token rows, rounded up to a 256-byte boundary; the segment records follow.
+static int64_t token_row_floats(const m3_scan_args& a) {
+  const bool rows = a.q_norm_w.data != nullptr || a.angles.data != nullptr;
+  if (!rows) return 0;
+  return ((int64_t)a.batch * a.length * ws_stride(a.rank, a.num_angles) + 63) / 64 * 64;
+}
+
+// Segment scratch: the state-pass records and the initial caches ([nseg][B][H][seg_rec] each),
+// then the block phase totals ([nseg][B][H][seg_len / 64][32]).
+static int64_t seg_floats(const m3_scan_args& a, const SegPlan& sp) {
+  if (sp.nseg <= 1) return 0;
+  const int64_t pairs = (int64_t)sp.nseg * a.batch * a.heads;
+  return 2 * pairs * seg_rec(a.rank) + pairs * (sp.seg_len / kPhaseBlock) * kMaxAngles;
+}
+
+static int64_t workspace_floats(const m3_scan_args& a) { return token_row_floats(a) + seg_floats(a, seg_plan(a)); }
+
 template <typename T, int R>
 static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
   // 16-byte vector stores of y need unit element stride and aligned row starts.
   auto even = [](int64_t s, int m) { return s % m == 0; };
   const int vec_y = a.y.stride[3] == 1 && aligned(a.y.data, 16) && even(a.y.stride[0], 8) &&
                     even(a.y.stride[1], 8) && even(a.y.stride[2], 8);
-  if (a.workspace.data) {
+  const bool token_rows = a.q_norm_w.data != nullptr || a.angles.data != nullptr;
+  const SegPlan sp = seg_plan(a);
+  SegArgs sg{sp.seg_len, sp.nseg, sp.seg_len / kPhaseBlock, nullptr, nullptr, nullptr};
+  if (sp.nseg > 1) {
+    const int64_t pairs = (int64_t)sp.nseg * a.batch * a.heads;
+    sg.part = static_cast<float*>(a.workspace.data) + token_row_floats(a);
+    sg.init = sg.part + pairs * seg_rec(R);
+    sg.blk = sg.init + pairs * seg_rec(R);
+  }
+  if (token_rows) {
     const int64_t tokens = (int64_t)a.batch * a.length;
     token_prep_kernel<T><<<(unsigned)((tokens + 7) / 8), 256, 0, stream>>>(a, static_cast<float*>(a.workspace.data));
     cudaError_t pe = cudaGetLastError();
@@ -1395,7 +1692,7 @@ static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
     if (!encode_rows(&tm.q, a.q, 5, dq, sq, bq) || !encode_rows(&tm.k, a.k, 5, dq, sk, bq) ||
         !encode_rows(&tm.x, a.value, 4, dx, sx, bx) || !encode_rows(&tm.z, a.gate, 4, dx, sz, bx))
       return cudaErrorInvalidValue;
-    if (a.workspace.data) {
+    if (token_rows) {
       PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
       const int W = ws_stride(R, a.num_angles);
       const cuuint64_t gdim[3] = {(cuuint64_t)W, (cuuint64_t)a.length, (cuuint64_t)a.batch};
@@ -1408,11 +1705,20 @@ static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
         return cudaErrorInvalidValue;
     }
   }
-  auto kern = scan_umma_kernel<T, R>;
   constexpr uint32_t smem = Layout<R>::SmemBytes;
+  if (sp.nseg > 1) {
+    auto pass1 = scan_umma_kernel<T, R, true>;
+    cudaError_t e = cudaFuncSetAttribute(pass1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    pass1<<<dim3(a.heads, a.batch, sp.nseg - 1), kThreads, smem, stream>>>(a, tm, vec_y, sg);
+    seg_combine_kernel<R><<<dim3(a.heads, a.batch), 256, 0, stream>>>(a, sg);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  auto kern = scan_umma_kernel<T, R, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(a.heads, a.batch), kThreads, smem, stream>>>(a, tm, vec_y);
+  kern<<<dim3(a.heads, a.batch, sp.nseg), kThreads, smem, stream>>>(a, tm, vec_y, sg);
   return cudaGetLastError();
 }
 
@@ -1429,10 +1735,10 @@ static cudaError_t launch_t(const m3_scan_args& a, cudaStream_t stream) {
 }  // namespace umma
 
 int64_t scan_umma_workspace_bytes(const m3_scan_args& a) {
-  const bool need = a.q_norm_w.data != nullptr || a.angles.data != nullptr;
-  if (!need) return 0;
-  return (int64_t)a.batch * a.length * umma::ws_stride(a.rank, a.num_angles) * (int64_t)sizeof(float);
+  return umma::workspace_floats(a) * (int64_t)sizeof(float);
 }
+
+int scan_umma_segments(const m3_scan_args& a) { return umma::seg_plan(a).nseg; }
 
 // Rows of q/k (N elements), value and gate (P elements) that start on 16-byte boundaries and are
 // contiguous, so the kernel can move them with 16-byte asynchronous copies.
@@ -1463,6 +1769,19 @@ bool scan_umma_supported(const m3_scan_args& a) {
          a.head_dim == umma::kP && (a.rank == 1 || a.rank == 2 || a.rank == 4 || a.rank == 8) &&
          (!has_phase || (a.mimo_rotation ? a.num_angles == umma::kMaxAngles : a.num_angles <= umma::kMaxAngles));
 }
+
+#ifdef M3_SECTION_TIMING
+// Probe builds only: per-section cycle totals of CTA (0, 0), thread 0, summed over launches.
+extern "C" int m3_probe_read_sections(unsigned long long* host16, int clear) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(host16, umma::g_section_cycles, 16 * sizeof(unsigned long long)) != cudaSuccess) return -1;
+  if (clear) {
+    unsigned long long zero[16] = {};
+    if (cudaMemcpyToSymbol(umma::g_section_cycles, zero, sizeof(zero)) != cudaSuccess) return -1;
+  }
+  return 0;
+}
+#endif
 
 cudaError_t launch_scan_umma(const m3_scan_args& a, cudaStream_t stream) {
   return a.value.dtype == M3_BF16 ? umma::launch_t<__nv_bfloat16>(a, stream) : umma::launch_t<__half>(a, stream);

@@ -316,6 +316,8 @@ __device__ __forceinline__ void store_state4(float* p, float4 v) {
 // i = l + 32 j; the cos/sin of a pair's angle comes from its owner lane by shuffle.
 template <typename T, int R, int NT>
 __global__ void __launch_bounds__(kStepThreads) step_prep_kernel(const m3_step_args a) {
+  // the stream pass may start now: it loads its state rows before it waits for this grid
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int64_t wid = (int64_t)blockIdx.x * (kStepThreads / 32) + (threadIdx.x >> 5);
   if (wid >= (int64_t)a.batch * a.heads) return;
@@ -472,6 +474,7 @@ __device__ __forceinline__ uint4 pack8(const float* v) {
 // sums of a row close within its 8 lanes; all row loads and stores are 16-byte vectors.
 template <typename T, int R>
 __global__ void __launch_bounds__(kStepThreads) step_prep_vec_kernel(const m3_step_args a) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   constexpr int N = 128, kUnits = 8 * R;
   constexpr bool kMimo = R > 1;
   const int lane = threadIdx.x & 31;
@@ -643,6 +646,9 @@ __global__ void __launch_bounds__(kStepThreads) step_stream_kernel(const m3_step
       sv[rr][v] = (p < P && n < N) ? load_state4(st + p * a.state.stride[2] + n) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
+  // Launched as a programmatic dependent of the prep pass: the state rows above do not depend on
+  // it, so their loads are in flight before this waits for the prep grid's workspace.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   float4 qv[R][NV], kv[R][NV], kpv[R][NV];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
@@ -822,9 +828,18 @@ static cudaError_t launch_step_two_pass(const m3_step_args& a, cudaStream_t stre
   const m3_tensor& pk = a.prev_k;
   const int vec_prev_k = sizeof(T) == 2 && pk.stride[3] == 1 && (reinterpret_cast<uintptr_t>(pk.data) & 7u) == 0 &&
                          pk.stride[0] % 4 == 0 && pk.stride[1] % 4 == 0 && pk.stride[2] % 4 == 0;
-  step_stream_kernel<T, R, NV, RPW><<<dim3((a.head_dim + rows - 1) / rows, a.heads, a.batch), kStepThreads, 0,
-                                      stream>>>(a, vec_prev_k);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the stream pass starts while the prep pass runs and waits for it
+  // (griddepcontrol.wait) only after issuing its state loads.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.head_dim + rows - 1) / rows, a.heads, a.batch);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, step_stream_kernel<T, R, NV, RPW>, a, vec_prev_k);
 }
 
 bool step_vec_ok(const m3_step_args& a) {
