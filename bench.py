@@ -444,6 +444,16 @@ def reference_gpu(workload, kernel_ms, layer_ms, steps=5):
         return {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
 
 
+def reference_gpu_all(configs: dict, head_workload: str, head: dict) -> dict:
+    """The reference Triton bar for every prefill configuration measured in this run (one layer
+    each, same per-GPU shape), beside our per-layer and scan-kernel times."""
+    out = {head_workload: reference_gpu(head_workload, head["roofline"]["kernel_ms"], head["layer_ms"])}
+    for wl, sub in configs.items():
+        if wl in WORKLOADS:
+            out[wl] = reference_gpu(wl, sub["roofline"]["kernel_ms"], sub["layer_ms"], steps=2)
+    return out
+
+
 def reference_gpu_decode(batch, our_us_per_layer, steps=64):
     """The reference's CUDA-graph decoder (its Triton step kernel) at the decode shape, depth 4,
     per layer beside ours."""
@@ -466,6 +476,59 @@ def reference_gpu_decode(batch, our_us_per_layer, steps=64):
                 "layer_speedup": us / depth / our_us_per_layer, "triton_dispatch": triton, "batch": batch}
     except Exception as exc:
         return {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+
+
+def cpu_config1() -> dict:
+    """BASELINE config 1 in full on the host cores with the reference's portable PyTorch path:
+    Mamba3(256, depth=4), fp32, manual_seed(0), x ~ N(0,1) [2, 1024, 256]: forward, then prefill of
+    the same x and 64 step() calls with fresh N(0,1) [2, 1, 256] inputs."""
+    try:
+        ref = import_reference()
+    except RuntimeError as exc:
+        return {"unavailable": str(exc)}
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    torch.manual_seed(0)
+    model = ref.Mamba3(256, d_state=128, depth=4, mimo_rank=1).eval()
+    x = torch.randn(2, 1024, 256)
+    steps = torch.randn(64, 2, 1, 256)
+    with torch.inference_mode():
+        model(x)
+        t0 = time.perf_counter()
+        model(x)
+        t1 = time.perf_counter()
+        _, cache = model.prefill(x)
+        t2 = time.perf_counter()
+        for i in range(64):
+            _, cache = model.step(steps[i], cache)
+        t3 = time.perf_counter()
+    return {"forward_ms": (t1 - t0) * 1e3, "forward_tokens_per_s": 2048 / (t1 - t0), "prefill_ms": (t2 - t1) * 1e3,
+            "step_ms": (t3 - t2) * 1e3 / 64, "cores": cores,
+            "impl": "reference mamba3 (baseline/_ref) portable PyTorch path on CPU tensors, fp32"}
+
+
+def gpu_config1() -> dict:
+    """The same config 1 through this package on the GPU (fp32: the CUDA-core scan kernel)."""
+    from mamba3_b200 import Mamba3
+    torch.manual_seed(0)
+    model = Mamba3(256, d_state=128, depth=4, mimo_rank=1).eval().cuda()
+    x = torch.randn(2, 1024, 256).cuda()
+    steps = torch.randn(64, 2, 1, 256).cuda()
+    with torch.inference_mode():
+        for _ in range(3):
+            model(x)
+        fwd = timed(lambda: model(x), 10, 1)
+        pre = timed(lambda: model.prefill(x), 10, 1)
+        _, cache = model.prefill(x)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record()
+        for i in range(64):
+            _, cache = model.step(steps[i], cache)
+        ev1.record()
+        torch.cuda.synchronize()
+    return {"forward_ms": fwd, "forward_tokens_per_s": 2048 / (fwd / 1e3), "prefill_ms": pre,
+            "step_ms": ev0.elapsed_time(ev1) / 64, "dtype": "f32"}
 
 
 def cpu_sample(workload, tokens=None) -> dict:
@@ -581,12 +644,18 @@ def main():
         result["configs"] = configs
         result["gpu_launches"] += sum(c.get("gpu_launches", 0) for c in configs.values())
     if rank == 0 and world == 1 and not args.no_ref_gpu and args.only is None:
-        result["reference_gpu"] = reference_gpu(args.workload, head["roofline"]["kernel_ms"], head["layer_ms"])
+        if "configs" in result:
+            result["reference_gpu"] = reference_gpu_all(result["configs"], args.workload, head)
+        else:
+            result["reference_gpu"] = {args.workload: reference_gpu(args.workload, head["roofline"]["kernel_ms"],
+                                                                    head["layer_ms"])}
         if "configs" in result:
             ours = result["configs"]["decode_b64"]["us_per_step"] / DECODE["depth"]
             result["reference_gpu_decode"] = reference_gpu_decode(64, ours)
     if rank == 0 and world == 1 and not args.no_cpu and args.only is None:
         result["cpu_baseline"] = cpu_sample(args.workload)
+        if not args.no_extras:
+            result["config1"] = {"gpu": gpu_config1(), "cpu_reference": cpu_config1()}
     if rank == 0:
         print(json.dumps(result))
     if world > 1:

@@ -90,8 +90,8 @@ constexpr uint32_t kOffST = kOffV2 + kRows * kP * 2;   // St [128 n][64 p]     1
 constexpr uint32_t kOffZ = kOffST + kN * kP * 2;       // z  [tokens][64] x 2 buffers (tile parity)
 constexpr uint32_t kOffF = kOffZ + 2 * kRows * kP * 2; // float region
 // float region (in floats): per-token scalars, then constants / workspace rows sized by the rank.
-constexpr int kSCum = 0, kSEcum = 64, kSEdec = 128, kSScale = 192, kSDiag = 256, kSDt = 320, kSWsum = 384,
-              kSCumL2 = 448, kSFq = 512, kSFk = 576, kSMode = 640, kSRaw = 656, kSEnd = 656 + 3 * 68;
+constexpr int kSEcum = 0, kSEdec = 64, kSDiag = 128, kSCumL2 = 192, kSFq = 256, kSFk = 320, kSMode = 384,
+              kSRaw = 400, kSEnd = 400 + 3 * 68;
 // Workspace floats per token: RMS factors of the q rows (R), of the k rows (R), then, from the next
 // 16-byte boundary, pi*tanh(angle) (S); padded to a multiple of 4 so each token's row is a run of
 // 16-byte chunks. Inside the kernel the angle slots are overwritten by the packed (cos, sin) words
@@ -108,9 +108,7 @@ template <int R> struct Layout {
   static_assert(CMz % 4 == 0 && CMo % 4 == 0, "16-byte aligned MIMO parameter rows");
   static constexpr int CWq = CMxp + R * kP / 2, CWk = CWq + kN / 2;   // packed norm weights [64]
   static constexpr int Ws = ((CWk + kN / 2 + 31) / 32) * 32;  // tile's workspace rows [TOK][WSP] (128 B)
-  static constexpr int Seg = Ws + TOK * WSP;            // [kWarps][32] sums, then [kWarps][32] offsets
-  static constexpr int Carry = Seg + 2 * kWarps * 32;   // [0..31] block offset, [32..63] within-block sum
-  static constexpr int FEnd = Carry + 64;
+  static constexpr int FEnd = Ws + TOK * WSP;
   static constexpr uint32_t OffBar = kOffF + ((FEnd * 4 + 15) / 16) * 16;  // mbarrier, tmem slot, abort flag
   static constexpr uint32_t SmemBytes = OffBar + 64 + 1024;                // + alignment slack
 };
@@ -142,6 +140,10 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   d |= (uint64_t)2 << 61;
   return d;
 }
+
+// Descriptor of the same tile `bytes` further on: the start-address field holds address / 16 in its
+// low 14 bits, and shared-memory addresses stay below 256 KB, so the field never carries over.
+__device__ __forceinline__ uint64_t sdesc_at(uint64_t d, uint32_t bytes) { return d + (uint64_t)(bytes >> 4); }
 
 // Instruction descriptor of tcgen05.mma kind::f16 with FP32 accumulation.
 __host__ __device__ constexpr uint32_t idesc(int m, int n, bool bf16, bool a_mn, bool b_mn) {
@@ -415,7 +417,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     scan_umma_kernel(const m3_scan_args a, const __grid_constant__ TileMaps tm, int vec_y, const SegArgs sg) {
   using Lay = Layout<R>;
   constexpr int TOK = Lay::TOK;
-  constexpr int kRowsPerWarp = kRows / kWarps;               // staging rows per warp (8)
   constexpr bool kBf16 = DType<T>::id == M3_BF16;
   // Largest |cum - cmid| for which the decay can be split into per-row operand factors
   // e^{cum_i - cmid} (Q rows) and e^{cmid - cum_j} (K rows) without leaving the 16-bit range.
@@ -435,12 +436,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* fsm = reinterpret_cast<float*>(smem + kOffF);
-  float* cum = fsm + kSCum;
   float* ecum = fsm + kSEcum;
   float* edec = fsm + kSEdec;
-  float* scale = fsm + kSScale;
   float* diag = fsm + kSDiag;
-  float* wsum = fsm + kSWsum;
   float* cum_l2 = fsm + kSCumL2;
   float* fq = fsm + kSFq;
   float* fk = fsm + kSFk;
@@ -535,20 +533,24 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       return;
     }
-    if (kStateOnly) return;
-    for (int c = tid; c < TOK * (kP / 8); c += kThreads) {
-      const int j = c >> 3, c8 = c & 7;
-      if (j < ntn) {
-        const int t = scan_token(a, t0n + j);
-        cp_async16(sbase + zoff + swz(j, c8 * 8, kRows), zp + z_b0 + (int64_t)t * a.gate.stride[1] + c8 * 8);
+    if constexpr (!kStateOnly) {
+      for (int c = tid; c < TOK * (kP / 8); c += kThreads) {
+        const int j = c >> 3, c8 = c & 7;
+        if (j < ntn) {
+          const int t = scan_token(a, t0n + j);
+          cp_async16(sbase + zoff + swz(j, c8 * 8, kRows), zp + z_b0 + (int64_t)t * a.gate.stride[1] + c8 * 8);
+        }
       }
     }
   };
-  // Per-token scalars of a tile: thread j <= TOK fetches the raw words of token j (j == TOK: the
-  // first token after the tile) into registers without using them, so the loads stay in flight;
-  // finish_scalars() converts them (softplus / heavy-tail / sigmoid) into sraw later.
+  // Per-token scalars of a tile: thread j <= TOK fetches the dt and decay words of token j (j == TOK:
+  // the first token after the tile) and thread 128 + j its trapezoid logit, into registers without
+  // using them, so the loads stay in flight; finish_scalars() converts them (softplus / heavy-tail on
+  // threads 0 .., sigmoid on threads 128 ..) into sraw later.
   uint32_t raw_dt = 0, raw_adt = 0, raw_trap = 0;
   bool raw_ok = false;
+  const int jt = tid >= 128 ? tid - 128 : tid;  // token of this thread's raw scalar
+  const bool trap_thread = tid >= 128;
   auto raw_word = [](const m3_tensor& t, int64_t idx) -> uint32_t {
     if (t.dtype == M3_F32) return __float_as_uint(static_cast<const float*>(t.data)[idx]);
     return (uint32_t)static_cast<const uint16_t*>(t.data)[idx];
@@ -560,18 +562,23 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
   auto fetch_scalars = [&](int t0n, int ntn) {
     raw_ok = false;
-    if (tid <= TOK && t0n + tid < L && (tid < ntn || tid == TOK)) {
-      const int t = scan_token(a, t0n + tid);
-      raw_dt = raw_word(a.dt, b * a.dt.stride[0] + (int64_t)t * a.dt.stride[1] + h * a.dt.stride[2]);
-      raw_adt = raw_word(a.adt, b * a.adt.stride[0] + (int64_t)t * a.adt.stride[1] + h * a.adt.stride[2]);
-      raw_trap = raw_word(a.trap, b * a.trap.stride[0] + (int64_t)t * a.trap.stride[1] + h * a.trap.stride[2]);
+    if (jt <= TOK && t0n + jt < L && (jt < ntn || jt == TOK)) {
+      const int t = scan_token(a, t0n + jt);
+      if (trap_thread) {
+        raw_trap = raw_word(a.trap, b * a.trap.stride[0] + (int64_t)t * a.trap.stride[1] + h * a.trap.stride[2]);
+      } else {
+        raw_dt = raw_word(a.dt, b * a.dt.stride[0] + (int64_t)t * a.dt.stride[1] + h * a.dt.stride[2]);
+        raw_adt = raw_word(a.adt, b * a.adt.stride[0] + (int64_t)t * a.adt.stride[1] + h * a.adt.stride[2]);
+      }
       raw_ok = true;
     }
   };
   const float dt_bias_h = a.dt_bias.data ? ld_t(a.dt_bias, h * a.dt_bias.stride[0]) : 0.0f;
   auto finish_scalars = [&]() {
-    if (tid <= TOK) {
-      float dtv = 0.0f, adtv = 0.0f, sg = 0.0f;
+    if (jt <= TOK && trap_thread) {
+      sraw[136 + jt] = raw_ok ? sigmoidf_(word_to_f(raw_trap, a.trap.dtype)) : 0.0f;
+    } else if (jt <= TOK) {
+      float dtv = 0.0f, adtv = 0.0f;
       if (raw_ok) {
         if (a.dt_bias.data) {
           // mamba3/model.py:195-198: dt = softplus(delta + dt_bias); A = -heavytail(a) clamped <= -1e-4.
@@ -581,11 +588,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           dtv = word_to_f(raw_dt, a.dt.dtype);
           adtv = word_to_f(raw_adt, a.adt.dtype);
         }
-        sg = sigmoidf_(word_to_f(raw_trap, a.trap.dtype));
       }
-      sraw[tid] = dtv;
-      sraw[68 + tid] = adtv;
-      sraw[136 + tid] = sg;
+      sraw[jt] = dtv;
+      sraw[68 + jt] = adtv;
     }
   };
   // Workspace rows (cp.async) or their stand-ins, and the phase tensor of the op-level API.
@@ -1142,14 +1147,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       M3_TMEM_LD32(tmem + lane_base + kColState + part * 32, r32);
       tmem_wait_ld();
       const int n = quad * 32 + lane;
+      if constexpr (!kStateOnly) {  // (the state pass has no inter-tile output term)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (kStateOnly) break;  // the state pass has no inter-tile output term
-        uint32_t w[4];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t w[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          w[i] = pack2<T>(__uint_as_float(r32[c * 8 + 2 * i]) * phi, __uint_as_float(r32[c * 8 + 2 * i + 1]) * phi);
-        *reinterpret_cast<uint4*>(smem + kOffST + swz(n, part * 32 + c * 8, kN)) = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int i = 0; i < 4; ++i)
+            w[i] = pack2<T>(__uint_as_float(r32[c * 8 + 2 * i]) * phi, __uint_as_float(r32[c * 8 + 2 * i + 1]) * phi);
+          *reinterpret_cast<uint4*>(smem + kOffST + swz(n, part * 32 + c * 8, kN)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
 #pragma unroll
       for (int j = 0; j < 32; ++j) r32[j] = __float_as_uint(__uint_as_float(r32[j]) * state_mult);
@@ -1162,30 +1168,34 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     M3_MARK(5);
 
-    // ---- MMA group 1: scores = Q' K'^T (committed on its own, so the W section starts as soon as
-    // they land), then inter = Q' St and X += K'^T V (or V2), which finish behind the W section ----
-    if (tid == 0) {
+    // ---- MMA group 1, issued by two threads at once (one thread issues a tcgen05.mma every ~60
+    // cycles; a second issuing warp doubles the rate). Thread 0: scores = Q' K'^T, committed on its own
+    // so the W section starts as soon as they land. Thread 32: the state update X += K'^T V (or V2),
+    // then inter = Q' St; both finish behind the W section. ----
+    if (tid == 0 && !kStateOnly) {
       fence_after();
-      if (!kStateOnly) {
+      const uint64_t dq = sdesc(sbase + kOffQ, 16, 1024), dk = sdesc(sbase + kOffK, 16, 1024);
 #pragma unroll
-        for (int kk = 0; kk < kN / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-          mma_f16(tmem + kColScores, sdesc(sbase + kOffQ + koff, 16, 1024), sdesc(sbase + kOffK + koff, 16, 1024),
-                  id_scores, kk > 0);
-        }
-        mma_commit(bar_addr);
-#pragma unroll
-        for (int kk = 0; kk < kN / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-          mma_f16(tmem + kColInter, sdesc(sbase + kOffQ + koff, 16, 1024),
-                  sdesc(sbase + kOffST + kk * 2048, kN * 128, 1024), id_nmn, kk > 0);
-        }
+      for (int kk = 0; kk < kN / 16; ++kk) {
+        const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+        mma_f16(tmem + kColScores, sdesc_at(dq, koff), sdesc_at(dk, koff), id_scores, kk > 0);
       }
-      const uint32_t vsrc = fact ? kOffV : kOffV2;
+      mma_commit(bar_addr);
+    }
+    if (tid == 32) {
+      fence_after();
+      const uint64_t dkm = sdesc(sbase + kOffK, kRows * 128, 1024);
+      const uint64_t dv = sdesc(sbase + (fact ? kOffV : kOffV2), kRows * 128, 1024);
 #pragma unroll
-      for (int kk = 0; kk < kRows / 16; ++kk) {
-        mma_f16(tmem + kColState, sdesc(sbase + kOffK + kk * 2048, kRows * 128, 1024),
-                sdesc(sbase + vsrc + kk * 2048, kRows * 128, 1024), id_state, 1);
+      for (int kk = 0; kk < kRows / 16; ++kk)
+        mma_f16(tmem + kColState, sdesc_at(dkm, kk * 2048), sdesc_at(dv, kk * 2048), id_state, 1);
+      if (!kStateOnly) {
+        const uint64_t dq = sdesc(sbase + kOffQ, 16, 1024), dst = sdesc(sbase + kOffST, kN * 128, 1024);
+#pragma unroll
+        for (int kk = 0; kk < kN / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
+          mma_f16(tmem + kColInter, sdesc_at(dq, koff), sdesc_at(dst, kk * 2048), id_nmn, kk > 0);
+        }
       }
       mma_commit(bar_b);
     }
@@ -1270,16 +1280,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---- MMA group 2: intra = W V ----
     if (tid == 0) {
       fence_after();
+      const uint64_t dw = sdesc(sbase + kOffW, 16, 1024), dv = sdesc(sbase + kOffV, kRows * 128, 1024);
 #pragma unroll
       for (int kk = 0; kk < kRows / 16; ++kk) {
         const uint32_t koff = (kk >> 2) * (kRows * 128) + (kk & 3) * 32;
-        mma_f16(tmem + kColIntra, sdesc(sbase + kOffW + koff, 16, 1024),
-                sdesc(sbase + kOffV + kk * 2048, kRows * 128, 1024), id_nmn, kk > 0);
+        mma_f16(tmem + kColIntra, sdesc_at(dw, koff), sdesc_at(dv, kk * 2048), id_nmn, kk > 0);
       }
       mma_commit(bar_c);
     }
-    // inter and the state update (issued before the W section) have finished: Q'/K' are free, so
-    // the next tile's raw q/k rows can start.
+    // the state update and inter (bar_b) and scores (with bar_c) have finished: Q'/K' are free, so the
+    // next tile's raw q/k rows can start.
     if (tid == 0 && !mbar_wait(bar_b, phase_bit)) *abort_flag = 1;
     if (use_tma) {
       if (ntn > 0) issue_qk(t0n, ntn);  // one thread issues the TMA boxes; the others skip
