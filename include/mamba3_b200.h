@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define M3_ABI_VERSION 2
+#define M3_ABI_VERSION 3
 
 enum m3_dtype { M3_F32 = 0, M3_F16 = 1, M3_BF16 = 2 };
 
@@ -83,7 +83,9 @@ typedef struct m3_tensor {
  */
 typedef struct m3_scan_args {
   int32_t batch, length, groups, heads, rank, d_state, head_dim, num_angles;
-  int32_t reverse;        /* 1: scan tokens L-1..0 (bidirectional backward direction) */
+  int32_t reverse;        /* 1: scan tokens L-1..0 (bidirectional backward direction); 2: both
+                             directions in one launch, forward into y, backward into y_reverse
+                             (the second read of each projection row is served from L2; no caches) */
   int32_t mimo_rotation;  /* 1: rotate pairs (i, 2S+i) (MIMO layout); 0: adjacent pairs (2i, 2i+1) */
   int32_t chunk_hint;     /* caller's chunk size (validated > 0; the kernel tiles internally) */
   int32_t device;         /* CUDA device ordinal of every tensor and of `stream` (-1: current) */
@@ -98,6 +100,7 @@ typedef struct m3_scan_args {
   m3_tensor initial_state, initial_k, initial_value;
   m3_tensor y, final_state, final_phase, final_k;
   m3_tensor workspace;
+  m3_tensor y_reverse;    /* [B,L,H,P] backward-direction output when reverse == 2 (same strides as y) */
 } m3_scan_args;
 
 /*
@@ -165,6 +168,24 @@ int64_t m3_scan_workspace_bytes(const m3_scan_args* args);
 /* Number of sequence segments the tensor-core scan kernel splits these sizes into (args->segments
  * and the GPU's SM count decide; 1 = no split). Negative: minus an M3_ERR_* code. */
 int m3_scan_segments(const m3_scan_args* args);
+
+/*
+ * Context-parallel prefill: summary of one rank's slice of a sequence (forward scans on the
+ * tensor-core layout). Runs the scan's state pass over the whole slice, starting from args' initial
+ * cache (or zeros) and phase 0 when no initial_phase is given, and writes per (batch, head) a record
+ * of m3_scan_summary_floats(rank) floats into `record` ([B][H][record]): the end state [P=64][N=128]
+ * at offset 0, the biased last k rotated by the slice's own phases [R][N] at offset 64*128 + 32,
+ * then the endpoint weight dt(1 - sigmoid(trap)) of the slice's first token and the slice's total
+ * log-decay sum(adt). With in-kernel phases (angles) the slice length must be a multiple of 64 and
+ * `blocks` ([B][H][L/64][32]) receives every 64-token block's in-block phase total, from which the
+ * block-offset carry (mamba3/model.py:246-251) continues across slices. Uses the workspace of
+ * m3_scan_workspace_bytes with args->segments = 1. No counterpart in the reference, which has no
+ * multi-GPU path; the state algebra is that of mamba3/ops.py:804-816.
+ */
+int m3_scan_summary(const m3_scan_args* args, float* record, float* blocks, void* stream);
+
+/* Floats per (batch, head) record written by m3_scan_summary for this MIMO rank. */
+int m3_scan_summary_floats(int rank);
 
 /* Fixed scratch size of m3_scan_fwd_noalloc, per GPU that loads the library: 8 MiB. */
 #define M3_NOALLOC_WORKSPACE_BYTES (8 * 1024 * 1024)

@@ -18,7 +18,7 @@ _LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libmamba3_b200.so"
 
 M3_F32, M3_F16, M3_BF16 = 0, 1, 2
 _DTYPES = {torch.float32: M3_F32, torch.float16: M3_F16, torch.bfloat16: M3_BF16}
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class M3Tensor(ctypes.Structure):
@@ -38,7 +38,7 @@ _SCAN_TENSORS = (
     "D", "mimo_x", "mimo_z", "mimo_out",
     "initial_state", "initial_k", "initial_value",
     "y", "final_state", "final_phase", "final_k",
-    "workspace",
+    "workspace", "y_reverse",
 )
 
 _STEP_TENSORS = (
@@ -112,6 +112,10 @@ def load() -> ctypes.CDLL:
         lib.m3_last_scan_kernel.restype = ctypes.c_char_p
         lib.m3_scan_segments.argtypes = [ctypes.POINTER(ScanArgs)]
         lib.m3_scan_segments.restype = ctypes.c_int
+        lib.m3_scan_summary.argtypes = [ctypes.POINTER(ScanArgs), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        lib.m3_scan_summary.restype = ctypes.c_int
+        lib.m3_scan_summary_floats.argtypes = [ctypes.c_int]
+        lib.m3_scan_summary_floats.restype = ctypes.c_int
         lib.m3_last_step_kernel.argtypes = []
         lib.m3_last_step_kernel.restype = ctypes.c_char_p
         if lib.m3_abi_version() != ABI_VERSION:
@@ -171,7 +175,7 @@ def scan_forward(*, sizes: dict, tensors: dict, reverse: bool = False, mimo_rota
     args.segments = _segments(segments)
     for key, val in sizes.items():
         setattr(args, key, int(val))
-    args.reverse = int(reverse)
+    args.reverse = 2 if reverse == "both" else int(reverse)
     args.mimo_rotation = int(mimo_rotation)
     args.chunk_hint = int(chunk_hint)
     args.norm_eps = float(norm_eps)
@@ -233,6 +237,46 @@ def residual_rmsnorm(x: torch.Tensor, m: torch.Tensor | None, w: torch.Tensor, e
     return out_n.view(x.shape)
 
 
+@torch.compiler.disable
+def scan_summary(*, sizes: dict, tensors: dict, mimo_rotation: bool = False, chunk_hint: int = 64,
+                 norm_eps: float = 1e-5) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Enqueue ``m3_scan_summary`` (the state pass of a whole slice, for context-parallel prefill).
+    Returns the records ``[B, H, m3_scan_summary_floats(R)]`` and, with in-kernel phases, the block
+    phase totals ``[B, H, L / 64, 32]`` (float32, on the tensors' device)."""
+    lib = load()
+    args = ScanArgs()
+    for key, val in sizes.items():
+        setattr(args, key, int(val))
+    args.segments = 1
+    args.mimo_rotation = int(mimo_rotation)
+    args.chunk_hint = int(chunk_hint)
+    args.norm_eps = float(norm_eps)
+    device = _cuda_device(tensors)
+    args.device = device.index if device.index is not None else torch.cuda.current_device()
+    for name in _SCAN_TENSORS:
+        setattr(args, name, _desc(tensors.get(name)))
+    need = lib.m3_scan_workspace_bytes(ctypes.byref(args))
+    if need < 0:
+        _check(int(-need), lib)
+    workspace = None
+    if need > 0:
+        workspace = torch.empty((need + 3) // 4, device=device, dtype=torch.float32)
+        args.workspace = _desc(workspace)
+    floats = lib.m3_scan_summary_floats(int(sizes["rank"]))
+    if floats < 0:
+        _check(int(-floats), lib)
+    batch, heads, length = int(sizes["batch"]), int(sizes["heads"]), int(sizes["length"])
+    record = torch.empty(batch, heads, floats, device=device, dtype=torch.float32)
+    blocks = None
+    if tensors.get("angles") is not None:
+        blocks = torch.empty(batch, heads, length // 64, 32, device=device, dtype=torch.float32)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _check(lib.m3_scan_summary(ctypes.byref(args), ctypes.c_void_p(record.data_ptr()),
+                               ctypes.c_void_p(blocks.data_ptr() if blocks is not None else 0),
+                               ctypes.c_void_p(stream)), lib)
+    return record, blocks
+
+
 def last_scan_kernel() -> str:
     return load().m3_last_scan_kernel().decode()
 
@@ -258,7 +302,7 @@ def scan_forward_noalloc(*, sizes: dict, tensors: dict, reverse: bool = False, m
     args.segments = _segments(segments)
     for key, val in sizes.items():
         setattr(args, key, int(val))
-    args.reverse = int(reverse)
+    args.reverse = 2 if reverse == "both" else int(reverse)
     args.mimo_rotation = int(mimo_rotation)
     args.chunk_hint = int(chunk_hint)
     args.norm_eps = float(norm_eps)

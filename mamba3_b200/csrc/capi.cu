@@ -16,6 +16,8 @@ size_t scan_simt_smem_bytes(int rank, int N, int P, int S);
 bool scan_umma_supported(const m3_scan_args& a);
 int64_t scan_umma_workspace_bytes(const m3_scan_args& a);
 int scan_umma_segments(const m3_scan_args& a);
+cudaError_t launch_scan_summary(const m3_scan_args& a, float* record, float* blocks, cudaStream_t stream);
+int scan_summary_record_floats(int rank);
 cudaError_t launch_scan_umma(const m3_scan_args& a, cudaStream_t stream);
 }  // namespace m3
 
@@ -153,6 +155,35 @@ int m3_scan_segments(const m3_scan_args* args) {
   return m3::scan_umma_segments(*args);
 }
 
+int m3_scan_summary_floats(int rank) {
+  if (rank != 1 && rank != 2 && rank != 4 && rank != 8) return -fail(M3_ERR_SHAPE, "rank must be 1, 2, 4 or 8");
+  return m3::scan_summary_record_floats(rank);
+}
+
+int m3_scan_summary(const m3_scan_args* args, float* record, float* blocks, void* stream) {
+  M3_REQUIRE(args != nullptr && record != nullptr, M3_ERR_ARGUMENT, "null argument");
+  m3_scan_args a = *args;
+  a.segments = 1;
+  M3_REQUIRE(a.batch > 0 && a.length > 0 && a.heads > 0 && a.groups > 0, M3_ERR_SHAPE,
+             "batch, length, heads and groups must be positive");
+  M3_REQUIRE(!a.reverse, M3_ERR_ARGUMENT, "sequence summaries are forward scans");
+  M3_REQUIRE(m3::scan_umma_supported(a), M3_ERR_LAYOUT,
+             "sequence summaries need the tensor-core scan layout (bf16/fp16, d_state 128, head_dim 64, "
+             "16-byte aligned contiguous rows)");
+  M3_REQUIRE(a.angles.data == nullptr || a.length % 64 == 0 || blocks == nullptr, M3_ERR_SHAPE,
+             "with in-kernel phases the summarised length must be a multiple of 64");
+  M3_REQUIRE(a.angles.data == nullptr || blocks != nullptr, M3_ERR_ARGUMENT,
+             "in-kernel phases need the block-total output");
+  const int64_t need = m3::scan_umma_workspace_bytes(a);
+  M3_REQUIRE(need == 0 || (present(a.workspace) && a.workspace.dtype == M3_F32), M3_ERR_ARGUMENT,
+             "a float32 workspace of m3_scan_workspace_bytes() bytes (segments = 1) is required");
+  const int dev_rc = select_device(a.device);
+  if (dev_rc != M3_OK) return dev_rc;
+  const cudaError_t e = m3::launch_scan_summary(a, record, blocks, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("summary launch failed: ") + cudaGetErrorString(e));
+  return M3_OK;
+}
+
 int m3_scan_fwd(const m3_scan_args* args, void* stream) {
   M3_REQUIRE(args != nullptr, M3_ERR_ARGUMENT, "null argument struct");
   const m3_scan_args& a = *args;
@@ -179,11 +210,20 @@ int m3_scan_fwd(const m3_scan_args* args, void* stream) {
       {&a.initial_k, "initial_k", 4, false}, {&a.initial_value, "initial_value", 3, false},
       {&a.y, "output", 4, true}, {&a.final_state, "final_state", 4, true},
       {&a.final_phase, "final_phase", 3, false}, {&a.final_k, "final_k", 4, false},
-      {&a.workspace, "workspace", 1, false},
+      {&a.workspace, "workspace", 1, false}, {&a.y_reverse, "y_reverse", 4, a.reverse == 2},
   };
   for (const Item& it : items) {
     const int rc = check_tensor(*it.t, it.name, it.nd, it.req);
     if (rc != M3_OK) return rc;
+  }
+  M3_REQUIRE(a.reverse >= 0 && a.reverse <= 2, M3_ERR_ARGUMENT, "reverse must be 0, 1 or 2");
+  if (a.reverse == 2) {
+    bool same = a.y_reverse.dtype == a.y.dtype;
+    for (int i = 0; i < 4; ++i) same = same && a.y_reverse.stride[i] == a.y.stride[i];
+    M3_REQUIRE(same, M3_ERR_LAYOUT, "y_reverse must have the dtype and strides of y");
+    M3_REQUIRE(!present(a.initial_state) && !present(a.initial_k) && !present(a.initial_phase) &&
+                   !present(a.final_phase) && !present(a.final_k),
+               M3_ERR_ARGUMENT, "the two-direction scan takes and returns no caches");
   }
   M3_REQUIRE(present(a.q_bias) == present(a.k_bias), M3_ERR_ARGUMENT, "q_bias and k_bias must be given together");
   M3_REQUIRE(present(a.q_norm_w) == present(a.k_norm_w), M3_ERR_ARGUMENT,
@@ -214,7 +254,17 @@ int m3_scan_fwd(const m3_scan_args* args, void* stream) {
     M3_REQUIRE(m3::scan_simt_smem_bytes(a.rank, a.d_state, a.head_dim, a.num_angles) <= 227 * 1024,
                M3_ERR_SHAPE, "d_state x head_dim too large for the scan kernel");
     g_last_scan_kernel = "simt";
-    e = m3::launch_scan_simt(a, s);
+    if (a.reverse == 2) {  // two launches: backward first, so the forward one writes final_state last
+      m3_scan_args bwd = a;
+      bwd.reverse = 1;
+      bwd.y = a.y_reverse;
+      m3_scan_args fwd = a;
+      fwd.reverse = 0;
+      e = m3::launch_scan_simt(bwd, s);
+      if (e == cudaSuccess) e = m3::launch_scan_simt(fwd, s);
+    } else {
+      e = m3::launch_scan_simt(a, s);
+    }
   }
   if (e != cudaSuccess) return fail(M3_ERR_CUDA, std::string("scan launch failed: ") + cudaGetErrorString(e));
   return M3_OK;

@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // Largest |cum - cmid| for which the decay can be split into per-row operand factors
   // e^{cum_i - cmid} (Q rows) and e^{cmid - cum_j} (K rows) without leaving the 16-bit range.
   constexpr float kLim = kBf16 ? 80.0f : 8.0f;
-  const int h = blockIdx.x, b = blockIdx.y, seg = blockIdx.z;
+  const int h = blockIdx.x, b = blockIdx.y, seg = a.reverse == 2 ? 0 : blockIdx.z;
   // This CTA's segment [seg_begin, L) in scan order; its end acts as the sequence end.
   const int seg_begin = seg * sg.seg_len;
   const int L = min(a.length, seg_begin + sg.seg_len);
@@ -456,7 +456,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   // them, bar_c the intra MMAs; each completes one phase per tile.
   const uint32_t bar_b = smem_u32(smem + Lay::OffBar + 32);
   const uint32_t bar_c = smem_u32(smem + Lay::OffBar + 40);
-  const bool use_tma = !a.reverse;
+  // Scan direction of this CTA: a.reverse = 1 scans tokens L-1 .. 0; a.reverse = 2 runs both
+  // directions in one launch (blockIdx.z = direction), so the two reads of a sequence's projections
+  // fall close together in time and the second is served from L2.
+  const bool rev = a.reverse == 1 || (a.reverse == 2 && blockIdx.z == 1);
+  auto tok = [&](int ts) { return rev ? a.length - 1 - ts : ts; };
+  const bool use_tma = !rev;
   const uint32_t bar_addr = smem_u32(bar);
   const uint32_t sbase = smem_u32(smem);
   const bool has_phase = a.phase.data != nullptr || a.angles.data != nullptr;
@@ -468,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const T* kp = static_cast<const T*>(a.k.data);
   const T* vp = static_cast<const T*>(a.value.data);
   const T* zp = static_cast<const T*>(a.gate.data);
-  T* yp = static_cast<T*>(a.y.data);
+  T* yp = static_cast<T*>(rev && a.reverse == 2 ? a.y_reverse.data : a.y.data);
   const float Dh = ld_t(a.D, h * a.D.stride[0]);
   // Row bases (the rows themselves are contiguous and 16-byte aligned: scan_umma_supported).
   const int64_t q_b0 = b * a.q.stride[0] + g * a.q.stride[2];
@@ -498,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int row = c >> 4, c8 = c & 15;
       const int j = row / R, r = row % R;
       if (j < ntn) {
-        const int t = scan_token(a, t0n + j);
+        const int t = tok(t0n + j);
         const uint32_t off = swz(row, c8 * 8, kRows);
         if (!kStateOnly)
           cp_async16(sbase + kOffQ + off, qp + q_b0 + (int64_t)t * a.q.stride[1] + r * a.q.stride[3] + c8 * 8);
@@ -517,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int c = tid; c < TOK * (kP / 8); c += kThreads) {
       const int j = c >> 3, c8 = c & 7;
       if (j < ntn) {
-        const int t = scan_token(a, t0n + j);
+        const int t = tok(t0n + j);
         cp_async16(sbase + (R == 1 ? kOffV : kOffW) + swz(j, c8 * 8, kRows),
                    vp + v_b0 + (int64_t)t * a.value.stride[1] + c8 * 8);
       }
@@ -537,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int c = tid; c < TOK * (kP / 8); c += kThreads) {
         const int j = c >> 3, c8 = c & 7;
         if (j < ntn) {
-          const int t = scan_token(a, t0n + j);
+          const int t = tok(t0n + j);
           cp_async16(sbase + zoff + swz(j, c8 * 8, kRows), zp + z_b0 + (int64_t)t * a.gate.stride[1] + c8 * 8);
         }
       }
@@ -563,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   auto fetch_scalars = [&](int t0n, int ntn) {
     raw_ok = false;
     if (jt <= TOK && t0n + jt < L && (jt < ntn || jt == TOK)) {
-      const int t = scan_token(a, t0n + jt);
+      const int t = tok(t0n + jt);
       if (trap_thread) {
         raw_trap = raw_word(a.trap, b * a.trap.stride[0] + (int64_t)t * a.trap.stride[1] + h * a.trap.stride[2]);
       } else {
@@ -602,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int c = tid; c < TOK * 16; c += kThreads) {
         const int j = c >> 4, c4 = c & 15;
         if (j < ntn && c4 < chunks) {
-          const int t = scan_token(a, t0n + j);
+          const int t = tok(t0n + j);
           cp_async16(smem_u32(wsb + j * WS + 4 * c4), ws + ws_b + (int64_t)t * WS + 4 * c4);
         }
       }
@@ -614,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int j = i / S, sidx = i % S;
         float v = 0.0f;
         if (j < ntn) {
-          const int t = scan_token(a, t0n + j);
+          const int t = tok(t0n + j);
           v = ld_t(a.phase, b * a.phase.stride[0] + (int64_t)t * a.phase.stride[1] + h * a.phase.stride[2] +
                                 sidx * a.phase.stride[3]);
         }
@@ -700,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       ist = m3_tensor{rec, M3_F32, 4, {sb, REC, kN, 1, 0, 0}};
       iph = m3_tensor{rec + kRecPhase, M3_F32, 3, {sb, REC, 1, 0, 0, 0}};
       ikt = m3_tensor{rec + kRecK, M3_F32, 4, {sb, REC, kN, 1, 0, 0}};
-      const int tprev = scan_token(a, seg_begin - 1);
+      const int tprev = tok(seg_begin - 1);
       ivt = m3_tensor{const_cast<T*>(vp) + (int64_t)tprev * a.value.stride[1], a.value.dtype, 3,
                       {a.value.stride[0], a.value.stride[2], a.value.stride[3], 0, 0, 0}};
     }
@@ -725,9 +730,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---- initial state into TMEM: S^T[n][p] = S0[p][n] + c0 sum_r (v mx_r)[p] k_r[n] ----
   {
     float c0 = 0.0f;
-    if (ikt.data || (kStateOnly && seg > 0)) {
+    if (ikt.data || kStateOnly) {
       float dt0, adt0;
-      const int t_first = scan_token(a, seg_begin);
+      const int t_first = tok(seg_begin);
       load_dt_adt(a, b, t_first, h, dt0, adt0);
       c0 = dt0 * (1.0f - sigmoidf_(load_trap(a, b, t_first, h)));
       // the state pass records the endpoint weight of its first token for the combine
@@ -1343,7 +1348,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       if (R == 1) {
         if (valid) {
-          const int t = scan_token(a, t0 + ti);
+          const int t = tok(t0 + ti);
           const int64_t ob = b * a.y.stride[0] + (int64_t)t * a.y.stride[1] + h * a.y.stride[2] +
                              (int64_t)p0 * a.y.stride[3];
           if (vec_y) {
@@ -1384,7 +1389,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         constexpr int kCols = 16 / R;
         if (valid) {
-          const int t = scan_token(a, t0 + ti);
+          const int t = tok(t0 + ti);
           const int64_t ob = b * a.y.stride[0] + (int64_t)t * a.y.stride[1] + h * a.y.stride[2] +
                              (int64_t)(p0 + cb) * a.y.stride[3];
           if (vec_y && kCols >= 2) {
@@ -1420,7 +1425,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   // ---- final state: S[p][n] = phi X^T ----
   fence_after();
-  if (!*abort_flag && (kStateOnly || last_seg)) {
+  if (!*abort_flag && (kStateOnly || last_seg) && !(a.reverse == 2 && rev)) {
     uint32_t r32[32];
     M3_TMEM_LD32(tmem + lane_base + kColState + part * 32, r32);
     tmem_wait_ld();
@@ -1634,6 +1639,7 @@ struct SegPlan {
 
 static SegPlan seg_plan(const m3_scan_args& a) {
   const int64_t L = a.length;
+  if (a.reverse == 2) return {1, (int)L};  // both directions in one launch: no split
   int want = 1;
   if (a.segments >= 2) {
     want = (int)std::min<int64_t>(a.segments, (L + 63) / 64);
@@ -1670,7 +1676,8 @@ static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
   // 16-byte vector stores of y need unit element stride and aligned row starts.
   auto even = [](int64_t s, int m) { return s % m == 0; };
   const int vec_y = a.y.stride[3] == 1 && aligned(a.y.data, 16) && even(a.y.stride[0], 8) &&
-                    even(a.y.stride[1], 8) && even(a.y.stride[2], 8);
+                    even(a.y.stride[1], 8) && even(a.y.stride[2], 8) &&
+                    (a.reverse != 2 || aligned(a.y_reverse.data, 16));
   const bool token_rows = a.q_norm_w.data != nullptr || a.angles.data != nullptr;
   const SegPlan sp = seg_plan(a);
   SegArgs sg{sp.seg_len, sp.nseg, sp.seg_len / kPhaseBlock, nullptr, nullptr, nullptr};
@@ -1689,7 +1696,7 @@ static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
   constexpr uint32_t TOK = Layout<R>::TOK;
   TileMaps tm;
   memset(&tm, 0, sizeof(tm));
-  if (!a.reverse) {
+  if (a.reverse != 1) {
     const uint64_t dq[5] = {(uint64_t)a.d_state, (uint64_t)R, (uint64_t)a.groups, (uint64_t)a.length,
                             (uint64_t)a.batch};
     const uint32_t bq[5] = {64, (uint32_t)R, 1, TOK, 1};
@@ -1728,8 +1735,69 @@ static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
   auto kern = scan_umma_kernel<T, R, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(a.heads, a.batch, sp.nseg), kThreads, smem, stream>>>(a, tm, vec_y, sg);
+  kern<<<dim3(a.heads, a.batch, a.reverse == 2 ? 2 : sp.nseg), kThreads, smem, stream>>>(a, tm, vec_y, sg);
   return cudaGetLastError();
+}
+
+// Summary of a whole sequence for a context-parallel caller: the state pass alone, run as one
+// segment from the caller's initial cache (or zeros), writing the segment record of every (batch,
+// head) into `record` [B][H][seg_rec(R)] and the 64-token block phase totals into `blocks`
+// [B][H][L / 64][32]. The workspace holds the per-token rows as for an unsplit scan.
+template <typename T, int R>
+static cudaError_t summary_r(const m3_scan_args& a, float* record, float* blocks, cudaStream_t stream) {
+  if (a.reverse) return cudaErrorInvalidValue;  // forward scans only
+  const bool token_rows = a.q_norm_w.data != nullptr || a.angles.data != nullptr;
+  SegArgs sg{a.length, 1, a.length / kPhaseBlock, record, nullptr, blocks};
+  if (token_rows) {
+    const int64_t tokens = (int64_t)a.batch * a.length;
+    token_prep_kernel<T><<<(unsigned)((tokens + 7) / 8), 256, 0, stream>>>(a, static_cast<float*>(a.workspace.data));
+    cudaError_t pe = cudaGetLastError();
+    if (pe != cudaSuccess) return pe;
+  }
+  TileMaps tm;
+  memset(&tm, 0, sizeof(tm));
+  {
+    constexpr uint32_t TOK = Layout<R>::TOK;
+    const uint64_t dq[5] = {(uint64_t)a.d_state, (uint64_t)R, (uint64_t)a.groups, (uint64_t)a.length,
+                            (uint64_t)a.batch};
+    const uint32_t bq[5] = {64, (uint32_t)R, 1, TOK, 1};
+    const int64_t sq[4] = {a.q.stride[3], a.q.stride[2], a.q.stride[1], a.q.stride[0]};
+    const int64_t sk[4] = {a.k.stride[3], a.k.stride[2], a.k.stride[1], a.k.stride[0]};
+    const uint64_t dx[4] = {(uint64_t)a.head_dim, (uint64_t)a.heads, (uint64_t)a.length, (uint64_t)a.batch};
+    const uint32_t bx[4] = {64, 1, TOK, 1};
+    const int64_t sx[3] = {a.value.stride[2], a.value.stride[1], a.value.stride[0]};
+    if (!encode_rows(&tm.q, a.q, 5, dq, sq, bq) || !encode_rows(&tm.k, a.k, 5, dq, sk, bq) ||
+        !encode_rows(&tm.x, a.value, 4, dx, sx, bx))
+      return cudaErrorInvalidValue;
+    if (token_rows) {
+      PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+      const int W = ws_stride(R, a.num_angles);
+      const cuuint64_t gdim[3] = {(cuuint64_t)W, (cuuint64_t)a.length, (cuuint64_t)a.batch};
+      const cuuint64_t gstr[2] = {(cuuint64_t)W * 4, (cuuint64_t)a.length * W * 4};
+      const cuuint32_t bdim[3] = {(cuuint32_t)W, TOK, 1}, estr[3] = {1, 1, 1};
+      if (enc == nullptr ||
+          enc(&tm.ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a.workspace.data, gdim, gstr, bdim, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    }
+  }
+  constexpr uint32_t smem = Layout<R>::SmemBytes;
+  auto pass1 = scan_umma_kernel<T, R, true>;
+  cudaError_t e = cudaFuncSetAttribute(pass1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  pass1<<<dim3(a.heads, a.batch, 1), kThreads, smem, stream>>>(a, tm, 0, sg);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t summary_t(const m3_scan_args& a, float* record, float* blocks, cudaStream_t stream) {
+  switch (a.rank) {
+    case 1: return summary_r<T, 1>(a, record, blocks, stream);
+    case 2: return summary_r<T, 2>(a, record, blocks, stream);
+    case 4: return summary_r<T, 4>(a, record, blocks, stream);
+    default: return summary_r<T, 8>(a, record, blocks, stream);
+  }
 }
 
 template <typename T>
@@ -1792,6 +1860,13 @@ extern "C" int m3_probe_read_sections(unsigned long long* host16, int clear) {
   return 0;
 }
 #endif
+
+cudaError_t launch_scan_summary(const m3_scan_args& a, float* record, float* blocks, cudaStream_t stream) {
+  return a.value.dtype == M3_BF16 ? umma::summary_t<__nv_bfloat16>(a, record, blocks, stream)
+                                  : umma::summary_t<__half>(a, record, blocks, stream);
+}
+
+int scan_summary_record_floats(int rank) { return umma::seg_rec(rank); }
 
 cudaError_t launch_scan_umma(const m3_scan_args& a, cudaStream_t stream) {
   return a.value.dtype == M3_BF16 ? umma::launch_t<__nv_bfloat16>(a, stream) : umma::launch_t<__half>(a, stream);

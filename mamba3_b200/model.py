@@ -83,7 +83,7 @@ class _Mamba3Mixer(nn.Module):
         # the cache tensor it was given (the decoder owns that cache).
         self._state_in_place = False
         # Autocast copies of the projection weights, kept across calls (see _project_linear).
-        self._weight_casts: dict[tuple[str, torch.dtype], tuple[int, int, torch.Tensor]] = {}
+        self._weight_casts: dict[tuple[str, torch.dtype], tuple] = {}
 
         width = 2 * self.d_inner + 2 * d_state * self.ngroups * mimo_rank + 3 * self.nheads + self.num_angles
         # Parameter creation order matches the reference so seeded initialisation is identical.
@@ -194,44 +194,51 @@ class _Mamba3Mixer(nn.Module):
 
     # ---- forward ----------------------------------------------------------------------------
 
-    def _scan_fused(self, projected: torch.Tensor, cache: _LayerCache | None, *, reverse: bool, want_cache: bool,
-                    heads: tuple[int, int] | None = None):
-        """One kernel launch for the whole SSD of this mixer (one direction), from raw projections.
+    def _scan_arguments(self, projected: torch.Tensor, cache: _LayerCache | None, heads: tuple[int, int] | None = None):
+        """Sizes, input tensors and flags of the kernel scan over raw ``in_proj`` columns (model mode).
         ``heads = (h0, h1)`` restricts it to those heads (head sharding): the per-head columns and
         parameters are sliced as views, q/k/angles are shared by every head."""
         z, x, B, C, delta, decay, trap, angles = self._views(projected)
         h0, h1 = heads if heads is not None else (0, self.nheads)
         hs = slice(h0, h1)
-        nh = h1 - h0
 
         def per_head(t):
             return None if t is None else t[hs]
 
         if heads is not None:
             z, x, delta, decay, trap = z[:, :, hs], x[:, :, hs], delta[..., hs], decay[..., hs], trap[..., hs]
-        batch, length = projected.shape[:2]
         act = projected.dtype
-        y = torch.empty(batch, length, nh, self.headdim, device=projected.device, dtype=act)
-        state = torch.empty(batch, nh, self.headdim, self.d_state, device=projected.device, dtype=torch.float32)
-        final_phase = final_k = None
-        if want_cache:
-            final_phase = torch.empty(batch, nh, self.num_angles, device=projected.device, dtype=torch.float32)
-            final_k = torch.empty(batch, nh, self.mimo_rank, self.d_state, device=projected.device, dtype=act)
         tensors = dict(q=C, k=B, q_norm_w=self.C_norm.weight, k_norm_w=self.B_norm.weight,
                        q_bias=per_head(self.C_bias), k_bias=per_head(self.B_bias), value=x, gate=z, adt=decay,
                        dt=delta, trap=trap, dt_bias=per_head(self.dt_bias), angles=angles, D=per_head(self.D),
                        mimo_x=per_head(self.mimo_x), mimo_z=per_head(self.mimo_z),
-                       mimo_out=per_head(self.mimo_out), y=y, final_state=state, final_phase=final_phase,
-                       final_k=final_k)
+                       mimo_out=per_head(self.mimo_out))
         if cache is not None:
             tensors.update(initial_phase=cache[0], initial_state=cache[1], initial_k=cache[2].to(act),
                            initial_value=cache[3].to(act))
-        sizes = dict(batch=batch, length=length, groups=self.ngroups, heads=nh, rank=self.mimo_rank,
-                     d_state=self.d_state, head_dim=self.headdim, num_angles=self.num_angles)
-        _ext.scan_forward(sizes=sizes, tensors=tensors, reverse=reverse, mimo_rotation=self.mimo_rank > 1,
-                          chunk_hint=self.inference_chunk_size, norm_eps=self.C_norm.eps)
+        sizes = dict(batch=projected.shape[0], length=projected.shape[1], groups=self.ngroups, heads=h1 - h0,
+                     rank=self.mimo_rank, d_state=self.d_state, head_dim=self.headdim, num_angles=self.num_angles)
+        kw = dict(mimo_rotation=self.mimo_rank > 1, chunk_hint=self.inference_chunk_size, norm_eps=self.C_norm.eps)
+        return sizes, tensors, kw
+
+    def _scan_fused(self, projected: torch.Tensor, cache: _LayerCache | None, *, reverse: bool, want_cache: bool,
+                    heads: tuple[int, int] | None = None):
+        """One kernel launch for the whole SSD of this mixer (one direction), from raw projections.
+        ``heads = (h0, h1)`` restricts it to those heads (head sharding)."""
+        sizes, tensors, kw = self._scan_arguments(projected, cache, heads)
+        batch, length, nh = sizes["batch"], sizes["length"], sizes["heads"]
+        act = projected.dtype
+        dev = projected.device
+        y = torch.empty(batch, length, nh, self.headdim, device=dev, dtype=act)
+        state = torch.empty(batch, nh, self.headdim, self.d_state, device=dev, dtype=torch.float32)
+        final_phase = final_k = None
+        if want_cache:
+            final_phase = torch.empty(batch, nh, self.num_angles, device=dev, dtype=torch.float32)
+            final_k = torch.empty(batch, nh, self.mimo_rank, self.d_state, device=dev, dtype=act)
+        tensors.update(y=y, final_state=state, final_phase=final_phase, final_k=final_k)
+        _ext.scan_forward(sizes=sizes, tensors=tensors, reverse=reverse, **kw)
         ops.LAST_SCAN_DISPATCH = True
-        return y, state, final_phase, final_k, x
+        return y, state, final_phase, final_k, tensors["value"]
 
     def mixed_heads(self, hidden_states: torch.Tensor, h0: int, h1: int, *, reverse: bool = False) -> torch.Tensor:
         """SSD output ``[B, L, h1 - h0, P]`` (before out_proj) of heads ``[h0, h1)`` for one direction:
@@ -268,17 +275,47 @@ class _Mamba3Mixer(nn.Module):
 
     def _forward_kernels(self, hidden_states, cache, return_cache):
         projected = self._project_linear("in_proj", hidden_states)
+        if not self.causal:
+            return self._forward_bidirectional_kernels(projected)
         mixed, state, phase, k_last, x = self._scan_fused(projected, cache, reverse=False, want_cache=return_cache)
         output = self._project_linear("out_proj", mixed.flatten(-2))
         if self.causal:
             if not return_cache:
                 return output
             return output, (phase, state, k_last, x[:, -1].clone())
-        # Backward direction: same projections read back to front, phase restarted at the end.
-        mixed_r, _, _, _, _ = self._scan_fused(projected, None, reverse=True, want_cache=False)
-        backward = self._project_linear("out_proj", mixed_r.flatten(-2))
-        blend = torch.sigmoid(self.direction_logit).to(output.dtype)
-        return output * blend + backward * (1.0 - blend)
+        raise AssertionError("unreachable: the bidirectional kernel path returns above")
+
+    def _forward_bidirectional_kernels(self, projected: torch.Tensor) -> torch.Tensor:
+        """Both directions of the bidirectional mixer (mamba3/model.py:333-362) in one scan launch
+        (``reverse="both"``: the backward CTAs read the projection rows the forward CTAs of the same
+        sequence pulled into L2), written side by side into one ``[B, L, 2, H, P]`` buffer, then the
+        blend and ``out_proj`` as one GEMM: ``out_proj(y_f) * w + out_proj(y_b) * (1 - w)`` equals
+        ``[y_f | y_b] @ [W diag(w) ; W diag(1 - w)]^T`` with w = sigmoid(direction_logit) per output
+        channel."""
+        sizes, tensors, kw = self._scan_arguments(projected, None)
+        batch, length = sizes["batch"], sizes["length"]
+        both = torch.empty(batch, length, 2, self.nheads, self.headdim, device=projected.device,
+                           dtype=projected.dtype)
+        state = torch.empty(batch, self.nheads, self.headdim, self.d_state, device=projected.device,
+                            dtype=torch.float32)
+        tensors.update(y=both[:, :, 0], y_reverse=both[:, :, 1], final_state=state)
+        _ext.scan_forward(sizes=sizes, tensors=tensors, reverse="both", **kw)
+        ops.LAST_SCAN_DISPATCH = True
+        return F.linear(both.flatten(-3), self._blended_out_weight(both.dtype))
+
+    def _blended_out_weight(self, dtype: torch.dtype) -> torch.Tensor:
+        """``[W diag(w) ; W diag(1 - w)]`` (out_proj weight W, w = sigmoid(direction_logit)), in the
+        activation dtype, rebuilt when either parameter changes."""
+        weight, logit = self.out_proj.weight, self.direction_logit
+        stamp = (weight.data_ptr(), weight._version, logit.data_ptr(), logit._version)
+        key = ("blend", dtype)
+        entry = self._weight_casts.get(key)
+        if entry is None or entry[:4] != stamp:
+            w = torch.sigmoid(logit.detach().float())[:, None]
+            blended = torch.cat((weight.detach().float() * w, weight.detach().float() * (1.0 - w)), dim=1)
+            entry = (*stamp, blended.to(dtype))
+            self._weight_casts[key] = entry
+        return entry[4]
 
     def _scan_torch_direction(self, hidden_states, cache):
         q, k, x, z, adt, dt, trap, angles = self._project(hidden_states)

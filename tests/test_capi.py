@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol():
 def test_struct_layout_matches_header():
     # 12 ints + float + int, then 26 tensor descriptors of 64 bytes.
     assert ctypes.sizeof(_ext.M3Tensor) == 64
-    assert ctypes.sizeof(_ext.ScanArgs) == 14 * 4 + 27 * 64
+    assert ctypes.sizeof(_ext.ScanArgs) == 14 * 4 + 28 * 64
     assert ctypes.sizeof(_ext.StepArgs) == 8 * 4 + 26 * 64
     assert ctypes.sizeof(_ext.NormArgs) == 8 + 4 * 4 + 5 * 64
 

@@ -309,3 +309,35 @@ def test_config1_forward_prefill_and_64_steps_fp32():
     for got, want in zip(cache, caches):
         for a, b in zip(got, want):
             assert rel_err(a, b) < 2e-4
+
+
+# ---------------------------------------------------------------------------------------------
+# Bidirectional mixer: both directions in one launch, blend folded into one out_proj GEMM
+# ---------------------------------------------------------------------------------------------
+
+def test_two_direction_scan_equals_two_launches_and_the_blend():
+    torch.manual_seed(0)
+    model = Mamba3(768, d_state=128, depth=1, causal=False).cuda().eval()
+    with torch.no_grad():
+        model.layers[0].mixer.direction_logit.normal_()
+    mixer = model.layers[0].mixer
+    x = torch.randn(2, 1000, 768, device="cuda")
+    with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+        proj = mixer._project_linear("in_proj", model.layers[0].norm(x))
+        fwd = mixer._scan_fused(proj, None, reverse=False, want_cache=False)
+        bwd = mixer._scan_fused(proj, None, reverse=True, want_cache=False)
+        sizes, tensors, kw = mixer._scan_arguments(proj, None)
+        both = torch.empty(2, 1000, 2, mixer.nheads, mixer.headdim, device="cuda", dtype=proj.dtype)
+        state = torch.empty_like(fwd[1])
+        tensors.update(y=both[:, :, 0], y_reverse=both[:, :, 1], final_state=state)
+        _ext.scan_forward(sizes=sizes, tensors=tensors, reverse="both", **kw)
+        assert _ext.last_scan_kernel() == "umma"
+        fused = mixer._forward_bidirectional_kernels(proj)
+        out = mixer._project_linear("out_proj", fwd[0].flatten(-2))
+        back = mixer._project_linear("out_proj", bwd[0].flatten(-2))
+        blend = torch.sigmoid(mixer.direction_logit).to(out.dtype)
+        unfused = out * blend + back * (1.0 - blend)
+    torch.testing.assert_close(both[:, :, 0], fwd[0], rtol=0, atol=0)
+    torch.testing.assert_close(both[:, :, 1], bwd[0], rtol=0, atol=0)
+    torch.testing.assert_close(state, fwd[1], rtol=0, atol=0)
+    assert rel_err(fused.float(), unfused.float()) < 2e-2

@@ -30,6 +30,9 @@ def _case(mode):
     from mamba3_b200 import Mamba3
 
     torch.manual_seed(0)
+    if mode.startswith("context"):  # one sequence of 150 tokens, split 128 + 22 along its length
+        model = Mamba3(32, d_state=16, depth=2, mimo_rank=4 if mode == "context_mimo" else 1).eval()
+        return model, torch.randn(2, 150, 32, generator=torch.Generator().manual_seed(1))
     if mode.startswith("heads"):
         model = Mamba3(96, d_state=16, depth=2, mimo_rank=2 if mode == "heads_mimo" else 1,
                        causal=mode != "heads_bidir").eval()
@@ -42,6 +45,7 @@ def _worker(rank, world, port, mode, out_dir):
     sys.path.insert(0, str(ROOT))
     import torch.distributed as dist
 
+    from mamba3_b200.context import forward_context_parallel
     from mamba3_b200.shard import forward_head_sharded, forward_sharded
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -52,7 +56,10 @@ def _worker(rank, world, port, mode, out_dir):
         if mode == "fail" and rank == 1:
             raise SystemExit(3)  # this rank dies before the gather
         with torch.no_grad():
-            y = (forward_head_sharded if mode.startswith("heads") else forward_sharded)(model, x)
+            if mode.startswith("context"):
+                y = forward_context_parallel(model, x[:, :128] if rank == 0 else x[:, 128:])
+            else:
+                y = (forward_head_sharded if mode.startswith("heads") else forward_sharded)(model, x)
         torch.save(y, Path(out_dir) / f"y{rank}.pt")
     except RuntimeError as error:  # the survivor's collective timed out / saw the peer close
         (Path(out_dir) / f"err{rank}.txt").write_text(str(error))
@@ -73,9 +80,10 @@ def test_shard_bounds_cover_the_batch_once():
         shard_bounds(4, 2, 2)
 
 
-@pytest.mark.parametrize("mode", ["siso", "mimo", "heads", "heads_mimo", "heads_bidir"])
+@pytest.mark.parametrize("mode", ["siso", "mimo", "heads", "heads_mimo", "heads_bidir", "context", "context_mimo"])
 def test_two_rank_sharded_forward_equals_single_process(tmp_path, mode):
-    """Batch sharding, and (modes "heads*") head sharding of a batch-1 input over 3 heads."""
+    """Batch sharding, (modes "heads*") head sharding of a batch-1 input over 3 heads, and (modes
+    "context*") context parallelism: each rank holds a slice of the sequence length."""
     port = _free_port()
     mp.start_processes(_worker, args=(2, port, mode, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
     model, x = _case(mode)
@@ -84,7 +92,11 @@ def test_two_rank_sharded_forward_equals_single_process(tmp_path, mode):
         expected = model(x)
     for rank in range(2):
         got = torch.load(tmp_path / f"y{rank}.pt")
-        torch.testing.assert_close(got, expected, rtol=1e-5, atol=1e-6)
+        if mode.startswith("context"):
+            want = expected[:, :128] if rank == 0 else expected[:, 128:]
+            torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-5)
+        else:
+            torch.testing.assert_close(got, expected, rtol=1e-5, atol=1e-6)
 
 
 def test_dead_rank_fails_the_gather_instead_of_hanging(tmp_path):
