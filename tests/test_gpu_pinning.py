@@ -192,7 +192,7 @@ def test_in_kernel_phase_at_length_131072(rank, target):
     # Each token's increment is rounded to float32 (tanhf, the product with dt, the fmod), so an
     # exact carry still drifts by up to ~2 ulp of |inc| per token; a broken carry or a missed block
     # reduction would be off by O(1) radians.
-    bound = 2e-3 + length * float(inc.abs().max()) * 2.0 ** -22
+    bound = 2e-3 + length * float(inc.detach().abs().max()) * 2.0 ** -22
     assert circ.abs().max() < bound
 
 
@@ -315,7 +315,10 @@ def test_config1_forward_prefill_and_64_steps_fp32():
 # Bidirectional mixer: both directions in one launch, blend folded into one out_proj GEMM
 # ---------------------------------------------------------------------------------------------
 
-def test_two_direction_scan_equals_two_launches_and_the_blend():
+def test_two_direction_scan_equals_two_launches_and_the_blend(monkeypatch):
+    # one segment everywhere: the two-direction launch never splits, the one-direction reference
+    # calls would split this small batch (the same result up to rounding, but not bit for bit)
+    monkeypatch.setenv("MAMBA3_B200_SEGMENTS", "1")
     torch.manual_seed(0)
     model = Mamba3(768, d_state=128, depth=1, causal=False).cuda().eval()
     with torch.no_grad():
