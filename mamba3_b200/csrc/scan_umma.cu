@@ -409,6 +409,16 @@ struct SegArgs {
   float* blk;    // state pass: in-block phase totals [nseg][B][H][nblk][32]
 };
 
+// softplus (torch threshold 20) and sigmoid of the per-token scalars with the hardware exp2/log2
+// approximations (relative error ~1e-6, far below the 16-bit rounding of every operand the kernel
+// stages); log(1 + e) is taken as e (1 - e / 2) below e = 1e-3, where 1 + e would round away e.
+__device__ __forceinline__ float softplus_fast(float x) {
+  if (x > 20.0f) return x;
+  const float e = __expf(x);
+  return e < 1e-3f ? e * (1.0f - 0.5f * e) : __logf(1.0f + e);
+}
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
 // x - 2pi * trunc(x / 2pi): the remainder of fmod (exact for |x| < 2pi, a few ulp beyond).
 __device__ __forceinline__ float fmod_2pi(float x) { return x - kTwoPi * truncf(x * (1.0f / kTwoPi)); }
 
@@ -421,7 +431,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   // Largest |cum - cmid| for which the decay can be split into per-row operand factors
   // e^{cum_i - cmid} (Q rows) and e^{cmid - cum_j} (K rows) without leaving the 16-bit range.
   constexpr float kLim = kBf16 ? 80.0f : 8.0f;
-  const int h = blockIdx.x, b = blockIdx.y, seg = a.reverse == 2 ? 0 : blockIdx.z;
+  // a.reverse == 2: both directions of a (batch, head) are adjacent CTAs (blockIdx.x = 2 h + dir),
+  // so they are resident together and the second reader of a projection row can hit L2.
+  const int h = a.reverse == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x, b = blockIdx.y;
+  const int seg = a.reverse == 2 ? 0 : blockIdx.z;
   // This CTA's segment [seg_begin, L) in scan order; its end acts as the sequence end.
   const int seg_begin = seg * sg.seg_len;
   const int L = min(a.length, seg_begin + sg.seg_len);
@@ -457,9 +470,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_b = smem_u32(smem + Lay::OffBar + 32);
   const uint32_t bar_c = smem_u32(smem + Lay::OffBar + 40);
   // Scan direction of this CTA: a.reverse = 1 scans tokens L-1 .. 0; a.reverse = 2 runs both
-  // directions in one launch (blockIdx.z = direction), so the two reads of a sequence's projections
+  // directions in one launch (blockIdx.x = 2 h + direction), so the two reads of a sequence's projections
   // fall close together in time and the second is served from L2.
-  const bool rev = a.reverse == 1 || (a.reverse == 2 && blockIdx.z == 1);
+  const bool rev = a.reverse == 1 || (a.reverse == 2 && (blockIdx.x & 1));
   auto tok = [&](int ts) { return rev ? a.length - 1 - ts : ts; };
   const bool use_tma = !rev;
   const uint32_t bar_addr = smem_u32(bar);
@@ -581,13 +594,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   const float dt_bias_h = a.dt_bias.data ? ld_t(a.dt_bias, h * a.dt_bias.stride[0]) : 0.0f;
   auto finish_scalars = [&]() {
     if (jt <= TOK && trap_thread) {
-      sraw[136 + jt] = raw_ok ? sigmoidf_(word_to_f(raw_trap, a.trap.dtype)) : 0.0f;
+      sraw[136 + jt] = raw_ok ? sigmoid_fast(word_to_f(raw_trap, a.trap.dtype)) : 0.0f;
     } else if (jt <= TOK) {
       float dtv = 0.0f, adtv = 0.0f;
       if (raw_ok) {
         if (a.dt_bias.data) {
           // mamba3/model.py:195-198: dt = softplus(delta + dt_bias); A = -heavytail(a) clamped <= -1e-4.
-          dtv = softplusf_(word_to_f(raw_dt, a.dt.dtype) + dt_bias_h);
+          dtv = softplus_fast(word_to_f(raw_dt, a.dt.dtype) + dt_bias_h);
           adtv = fminf(-heavy_tailf(word_to_f(raw_adt, a.adt.dtype)), -kAFloor) * dtv;
         } else {
           dtv = word_to_f(raw_dt, a.dt.dtype);
@@ -1735,7 +1748,7 @@ static cudaError_t launch_r(const m3_scan_args& a, cudaStream_t stream) {
   auto kern = scan_umma_kernel<T, R, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<dim3(a.heads, a.batch, a.reverse == 2 ? 2 : sp.nseg), kThreads, smem, stream>>>(a, tm, vec_y, sg);
+  kern<<<dim3(a.reverse == 2 ? 2 * a.heads : a.heads, a.batch, a.reverse == 2 ? 1 : sp.nseg), kThreads, smem, stream>>>(a, tm, vec_y, sg);
   return cudaGetLastError();
 }
 
