@@ -3,32 +3,36 @@
 // Shapes served: bf16/fp16 activations, d_state N = 128, head_dim P = 64, any rank R in
 // {1, 2, 4, 8}, up to 32 rotation angles. A pre-pass (token_prep_kernel) computes the per-token
 // values every head shares — RMS factors of the q/k rows and pi*tanh(angle) — once into the
-// caller's workspace. Then one CTA (512 threads) owns one (batch, head) pair and
-// walks the sequence in tiles of 128 flattened (token, rank) rows (128 / R tokens), keeping the
-// FP32 state S^T [N=128, P=64] resident in tensor memory for the whole sequence.
+// caller's workspace. Then one CTA (256 threads, 8 warps; two CTAs per SM) owns one
+// (batch, head[, segment]) and walks its tokens in tiles of 64 flattened (token, rank) rows
+// (64 / R tokens), keeping the FP32 state S^T [N=128, P=64] resident in tensor memory.
 //
 // Per tile (mamba3/ops.py:716-816 math; mamba3/_triton.py:74-413 is the reference's fused form):
-//   stage   Q  = rot(norm(C) + C_bias)            [128 rows, 128]  bf16, K-major   (smem)
-//           K  = rot(norm(B) + B_bias) * scale    [128 rows, 128]  bf16            (smem)
-//           V  = x * mimo_x                       [128 rows, 64]   bf16            (smem)
-//           V2 = V * e^{cum_last - cum}           [128 rows, 64]   bf16            (smem)
-//           St = bf16(S^T) (state before tile)    [128 n, 64 p]    bf16            (smem)
-//           TMEM S^T <- e^{cum_last} S^T
-//   MMA 1   scores = Q K^T          -> TMEM [128 x 128] f32
-//   MMA 2   Y_inter = Q St          -> TMEM [128 x 64]  f32    (B operand MN-major)
-//   MMA 3   S^T += K^T V2           -> TMEM [128 x 64]  f32    (A and B operands MN-major)
-//   W       = scores o decay (exp of cum differences below the diagonal, gamma/scale on same-token
-//             pairs, 0 above), rounded to bf16 -> smem, K-major
-//   MMA 4   Y_intra = W V           -> TMEM [128 x 64]  f32
-//   epilogue y = e^{cum} Y_inter + Y_intra + D v, SiLU(z mz) gate, MIMO rank sum -> global
+//   stage   Q' = rot(norm(C) + C_bias) e^{cum - cmid}           [64 rows, 128] 16-bit, K-major
+//           K' = rot(norm(B) + B_bias) scale e^{cmid - cum}     [64 rows, 128] 16-bit
+//           V  = x mimo_x                                        [64 rows, 64]
+//           V2 = V e^{cum_last - cum}  (only tiles whose decay range is too wide to factorise)
+//           St = 16-bit copy of the state before the tile        [128 n, 64 p]
+//           TMEM state rescaled by the tile's decay
+//   MMA g1  scores = Q' K'^T   -> TMEM [64 x 64]  f32   (M = 64)
+//           S^T   += K'^T V    -> TMEM [128 x 64] f32   (M = 128, A and B MN-major)
+//           inter  = Q' St     -> TMEM [64 x 64]  f32   (B operand MN-major)
+//   W       = causal mask of the scores (gamma/scale on same-token pairs, D on the diagonal,
+//             exact per-element decay on unfactorised tiles), 16-bit -> smem, K-major
+//   MMA g2  intra = W V        -> TMEM [64 x 64]  f32
+//   epilogue y = e^{cmid} inter + intra, SiLU(z mz) gate, mimo_out rank sum -> global
+//
+// Long sequences with few (batch, head) pairs are split into segments: a state-only pass per
+// segment, an FP32 scan over the segment records (seg_combine_kernel), then the main pass with
+// every segment started from its true initial state.
 //
 // All operand tiles use the 128-byte swizzled canonical layout: a tile of `rows` x `cols`
 // 16-bit elements is stored as cols/64 column blocks of rows x 128 B; inside a block, row r,
 // 16-byte chunk c lives at r*128 + ((c ^ (r & 7)) * 16). The same bytes serve as a K-major
 // operand ([MN rows][K cols]) or as an MN-major one ([K rows][MN cols]).
 //
-// Synchronisation: one mbarrier tracks tcgen05.commit of each MMA group; every wait on it is
-// bounded by %globaltimer (2 s) and sets the library's device error word instead of hanging.
+// Synchronisation: mbarriers track the TMA loads and tcgen05.commit of each MMA group; every wait
+// is bounded by %globaltimer (2 s) and sets the library's device error word instead of hanging.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
