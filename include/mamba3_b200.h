@@ -187,6 +187,42 @@ int m3_scan_summary(const m3_scan_args* args, float* record, float* blocks, void
 /* Floats per (batch, head) record written by m3_scan_summary for this MIMO rank. */
 int m3_scan_summary_floats(int rank);
 
+/*
+ * Training kernels of the chunked SSD core (the gradients the reference's training path takes by
+ * autograd through mamba3/ops.py:716-816, with the _BmmFloat GEMMs of ops.py:202-250). The core
+ * op, per (batch, head), rows i = (token t, rank r), chunks of m3_ssd_chunk_rows() rows:
+ *   y_i = e^{cum_t} (S_c q_i) + sum_{j in chunk, token(j) <= t} Wt_ij v_j,
+ *   Wt_ij = e^{cum_t - cum_s} (q_i . k_j) for earlier tokens s, diag_t (q_i . k_j) on token t,
+ *   S_{c+1} = e^{cum_last} S_c + sum_j e^{cum_last - cum_s} v_j k_j^T,
+ * cum = inclusive cumsum of adt inside the chunk. All tensors float32 with element strides:
+ *   q, k [B,L,H,R,N] (k already times the trapezoid scale), v [B,L,H,R,P] (rank values),
+ *   adt, diag [B,L,H], initial_state / final_state / dfinal / dinitial [B,H,P,N],
+ *   y / dy [B,L,H,R,P], chunk_states [B,H,ceil(L*R/rows),P,N] (written by the forward, read by
+ *   the backward), dq, dk [B,L,H,R,N], dv [B,L,H,R,P], dadt, ddiag [B,L,H].
+ * d_state <= 128, head_dim <= 64. initial_state, dfinal and dinitial may be null (zeros / not
+ * written). The bias, rotation, scale, D skip, gate and rank sum around the core are left to the
+ * caller's autograd.
+ */
+typedef struct m3_ssd_args {
+  int32_t batch, length, heads, rank, d_state, head_dim;
+  int32_t device; /* CUDA device ordinal of every tensor and of `stream` (-1: current) */
+  int32_t reserved;
+  m3_tensor q, k, v, adt, diag, initial_state;
+  m3_tensor y, final_state, chunk_states;
+  m3_tensor dy, dfinal;
+  m3_tensor dq, dk, dv, dadt, ddiag, dinitial;
+} m3_ssd_args;
+
+/* Rows (token, rank) per chunk of the training kernels. */
+int m3_ssd_chunk_rows(void);
+
+/* Forward of the SSD core for training: y, final_state and chunk_states. M3_OK or M3_ERR_*. */
+int m3_ssd_train_fwd(const m3_ssd_args* args, void* stream);
+
+/* Backward of the SSD core: dq, dk, dv, dadt, ddiag (and dinitial when given) from dy (and dfinal
+ * when given), q, k, v, adt, diag and the forward's chunk_states. M3_OK or M3_ERR_*. */
+int m3_ssd_train_bwd(const m3_ssd_args* args, void* stream);
+
 /* Fixed scratch size of m3_scan_fwd_noalloc, per GPU that loads the library: 8 MiB. */
 #define M3_NOALLOC_WORKSPACE_BYTES (8 * 1024 * 1024)
 

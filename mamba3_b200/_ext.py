@@ -72,6 +72,20 @@ class StepArgs(ctypes.Structure):
         (name, M3Tensor) for name in _STEP_TENSORS]
 
 
+_SSD_TENSORS = (
+    "q", "k", "v", "adt", "diag", "initial_state",
+    "y", "final_state", "chunk_states",
+    "dy", "dfinal",
+    "dq", "dk", "dv", "dadt", "ddiag", "dinitial",
+)
+
+
+class SSDArgs(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int32) for name in (
+        "batch", "length", "heads", "rank", "d_state", "head_dim", "device", "reserved")] + [
+        (name, M3Tensor) for name in _SSD_TENSORS]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -118,6 +132,12 @@ def load() -> ctypes.CDLL:
         lib.m3_scan_summary_floats.restype = ctypes.c_int
         lib.m3_last_step_kernel.argtypes = []
         lib.m3_last_step_kernel.restype = ctypes.c_char_p
+        lib.m3_ssd_chunk_rows.argtypes = []
+        lib.m3_ssd_chunk_rows.restype = ctypes.c_int
+        lib.m3_ssd_train_fwd.argtypes = [ctypes.POINTER(SSDArgs), ctypes.c_void_p]
+        lib.m3_ssd_train_fwd.restype = ctypes.c_int
+        lib.m3_ssd_train_bwd.argtypes = [ctypes.POINTER(SSDArgs), ctypes.c_void_p]
+        lib.m3_ssd_train_bwd.restype = ctypes.c_int
         if lib.m3_abi_version() != ABI_VERSION:
             raise RuntimeError("mamba3_b200 library ABI mismatch; rebuild it")
         _lib = lib
@@ -312,3 +332,56 @@ def scan_forward_noalloc(*, sizes: dict, tensors: dict, reverse: bool = False, m
         setattr(args, name, _desc(tensors.get(name)))
     stream = torch.cuda.current_stream(device).cuda_stream
     _check(lib.m3_scan_fwd_noalloc(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
+
+
+def _ssd_args(q: torch.Tensor, tensors: dict) -> SSDArgs:
+    batch, length, heads, rank, d_state = q.shape
+    args = SSDArgs()
+    args.batch, args.length, args.heads, args.rank, args.d_state = batch, length, heads, rank, d_state
+    args.head_dim = tensors["v"].shape[-1]
+    args.device = q.device.index if q.device.index is not None else torch.cuda.current_device()
+    for name in _SSD_TENSORS:
+        setattr(args, name, _desc(tensors.get(name)))
+    return args
+
+
+@torch.compiler.disable
+def ssd_train_forward(q, k, v, adt, diag, initial_state):
+    """``m3_ssd_train_fwd``: the SSD core for training on float32 tensors ``q, k [B,L,H,R,N]``,
+    ``v [B,L,H,R,P]``, ``adt, diag [B,L,H]``, ``initial_state [B,H,P,N]`` (or None). Returns
+    ``(y [B,L,H,R,P], final_state [B,H,P,N], chunk_states)`` (float32)."""
+    lib = load()
+    batch, length, heads, rank, d_state = q.shape
+    head_dim = v.shape[-1]
+    rows = lib.m3_ssd_chunk_rows()
+    nchunk = (length * rank + rows - 1) // rows
+    dev = q.device
+    y = torch.empty(batch, length, heads, rank, head_dim, device=dev, dtype=torch.float32)
+    final = torch.empty(batch, heads, head_dim, d_state, device=dev, dtype=torch.float32)
+    chunks = torch.empty(batch, heads, nchunk, head_dim, d_state, device=dev, dtype=torch.float32)
+    args = _ssd_args(q, dict(q=q, k=k, v=v, adt=adt, diag=diag, initial_state=initial_state, y=y,
+                             final_state=final, chunk_states=chunks))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _check(lib.m3_ssd_train_fwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
+    return y, final, chunks
+
+
+@torch.compiler.disable
+def ssd_train_backward(q, k, v, adt, diag, chunk_states, dy, dfinal, want_initial: bool):
+    """``m3_ssd_train_bwd``: gradients ``(dq, dk, dv, dadt, ddiag, dinitial or None)`` of the SSD
+    core from ``dy [B,L,H,R,P]`` and ``dfinal [B,H,P,N]`` (or None), float32."""
+    lib = load()
+    batch, length, heads, rank, d_state = q.shape
+    head_dim = v.shape[-1]
+    dev = q.device
+    dq, dk = torch.empty_like(q), torch.empty_like(k)
+    dv = torch.empty_like(v)
+    dadt = torch.empty(batch, length, heads, device=dev, dtype=torch.float32)
+    ddiag = torch.empty_like(dadt)
+    dinit = (torch.empty(batch, heads, head_dim, d_state, device=dev, dtype=torch.float32)
+             if want_initial else None)
+    args = _ssd_args(q, dict(q=q, k=k, v=v, adt=adt, diag=diag, chunk_states=chunk_states, dy=dy, dfinal=dfinal,
+                             dq=dq, dk=dk, dv=dv, dadt=dadt, ddiag=ddiag, dinitial=dinit))
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _check(lib.m3_ssd_train_bwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
+    return dq, dk, dv, dadt, ddiag, dinit

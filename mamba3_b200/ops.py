@@ -6,9 +6,11 @@ jreoka/mamba3): :func:`heavy_tail_activation`, :func:`rotate_qk`, :func:`fused_s
 
 Dispatch rule. Inference calls on CUDA tensors (no tensor that requires grad while grad mode is
 on) run the sm_100a kernels of ``csrc/`` through the C ABI — there is no other GPU path and no
-silent fallback: if the library is missing the call raises. Calls that need autograd, and calls on
-CPU tensors, run the PyTorch formulation below (the training path and the CPU device path, as in
-the reference, ``mamba3/ops.py:659-822``).
+silent fallback: if the library is missing the call raises. Calls on CUDA tensors that need
+autograd (training) run the chunked core on the training kernels (``m3_ssd_train_fwd/bwd``) with
+the elementwise prelude and epilogue as PyTorch ops (d_state <= 128 and head_dim <= 64; other shapes
+take the PyTorch formulation). Calls on CPU tensors run the PyTorch formulation below (the CPU
+device path, as in the reference, ``mamba3/ops.py:659-822``).
 """
 
 from __future__ import annotations
@@ -227,6 +229,73 @@ def _scan_torch(q, k, value, gate, adt, dt, trap_logits, D, *, mimo_x, mimo_z, m
     return torch.cat(outputs, dim=1), state
 
 
+class _SSDCore(torch.autograd.Function):
+    """The chunked SSD core on the training kernels (``m3_ssd_train_fwd`` / ``m3_ssd_train_bwd``):
+    ``(q, k*scale, rank values, adt, diag, initial state) -> (pre-gate output [B,L,H,R,P], final
+    state)``, float32. The forward keeps the state at every chunk start for the backward."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, adt, diag, initial_state):
+        y, final, chunks = _ext.ssd_train_forward(q, k, v, adt, diag, initial_state)
+        ctx.save_for_backward(q, k, v, adt, diag, chunks)
+        return y, final
+
+    @staticmethod
+    def backward(ctx, dy, dfinal):
+        q, k, v, adt, diag, chunks = ctx.saved_tensors
+        dy = torch.zeros_like(v) if dy is None else dy.float().contiguous()
+        dfinal = None if dfinal is None else dfinal.float().contiguous()
+        dq, dk, dv, dadt, ddiag, dinit = _ext.ssd_train_backward(q, k, v, adt, diag, chunks, dy, dfinal,
+                                                                 want_initial=ctx.needs_input_grad[5])
+        return dq, dk, dv, dadt, ddiag, dinit
+
+
+def _train_kernel_eligible(q, value) -> bool:
+    """CUDA autograd calls whose shapes the training kernels serve (d_state <= 128, head_dim <= 64)."""
+    return q.is_cuda and q.shape[-1] <= 128 and value.shape[-1] <= 64
+
+
+def _scan_train(q, k, value, gate, adt, dt, trap_logits, D, *, mimo_x, mimo_z, mimo_out, chunk_size,
+                initial_state, initial_k, initial_value, phase, mimo_rotation, q_bias, k_bias):
+    """Differentiable chunked SSD for CUDA training: the same prelude as :func:`_scan_torch` (group
+    expansion, bias, rotation, trapezoid scale, rank values, endpoint-cache term) as PyTorch ops,
+    the chunked core and its backward on the training kernels, then D skip, SiLU gate and rank sum.
+    The core runs in float32 from the activation-dtype operands (no intermediate 16-bit rounding)."""
+    heads = value.shape[2]
+    act = value.dtype
+    qf = _expand_groups(q, heads)
+    kf = _expand_groups(k, heads)
+    if q_bias is not None:
+        qf = qf + q_bias.to(q.dtype)
+        kf = kf + k_bias.to(k.dtype)
+    if phase is not None:
+        qf, kf = rotate_qk(qf, kf, phase, mimo=mimo_rotation)
+    sig, _, scale, diag = _scalar_prelude(adt, dt, trap_logits)
+    kc = kf * scale.to(k.dtype)[..., None, None]
+
+    def rank_act(t, proj):  # [..., H, P] -> [..., H, R, P] in the activation dtype (ops.py:193-199)
+        return t.unsqueeze(-2) if proj is None else t.unsqueeze(-2) * proj.to(t.dtype)
+
+    rv = rank_act(value, mimo_x)
+    rz = rank_act(gate, mimo_z)
+    state = None if initial_state is None else initial_state.float()
+    if initial_k is not None:
+        prev = rank_act(initial_value, mimo_x).float()
+        coef = dt.float()[:, 0] * (1.0 - sig[:, 0])
+        outer = coef[..., None, None] * torch.einsum("bhrp,bhrn->bhpn", prev, initial_k.float())
+        state = outer if state is None else state + outer
+    # the kernels compute in float32 (a float64 caller off the GPU keeps float64: host-logic checks)
+    cdt = torch.float32 if q.is_cuda else torch.promote_types(act, torch.float32)
+    rvf = rv.to(cdt)
+    if state is not None:
+        state = state.to(cdt)
+    y, final = _SSDCore.apply(qf.to(cdt).contiguous(), kc.to(cdt).contiguous(), rvf.contiguous(),
+                              adt.to(cdt).contiguous(), diag.to(cdt).contiguous(), state)
+    y = (y + D.to(cdt)[:, None, None] * rvf) * F.silu(rz.to(cdt))
+    y = y.sum(dim=3) if mimo_out is None else (y * mimo_out.to(cdt)).sum(dim=3)
+    return y.to(act), final
+
+
 def _scan_device(q, k, value, gate, adt, dt, trap_logits, D, *, mimo_x, mimo_z, mimo_out, chunk_size,
                  initial_state, initial_k, initial_value, phase, mimo_rotation, q_bias, k_bias):
     batch, length, groups, rank, d_state = q.shape
@@ -277,6 +346,10 @@ def mamba3_scan(q, k, value, gate, adt, dt, trap_logits, D, *, mimo_x=None, mimo
                initial_value, phase, q_bias, k_bias)
     if _kernel_eligible(*tensors):
         out = _scan_device(q, k, value, gate, adt, dt, trap_logits, D, **kwargs)
+        LAST_SCAN_DISPATCH = True
+        return out
+    if _train_kernel_eligible(q, value) and _needs_autograd(*tensors):
+        out = _scan_train(q, k, value, gate, adt, dt, trap_logits, D, **kwargs)
         LAST_SCAN_DISPATCH = True
         return out
     return _scan_torch(q, k, value, gate, adt, dt, trap_logits, D, **kwargs)
