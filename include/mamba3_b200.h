@@ -199,8 +199,10 @@ int m3_scan_summary_floats(int rank);
  *   adt, diag [B,L,H], initial_state / final_state / dfinal / dinitial [B,H,P,N],
  *   y / dy [B,L,H,R,P], chunk_states [B,H,ceil(L*R/rows),P,N] (written by the forward, read by
  *   the backward), dq, dk [B,L,H,R,N], dv [B,L,H,R,P], dadt, ddiag [B,L,H].
- * d_state <= 128, head_dim <= 64. initial_state, dfinal and dinitial may be null (zeros / not
- * written). The bias, rotation, scale, D skip, gate and rank sum around the core are left to the
+ * d_state <= 128 and head_dim <= 64, multiples of 8. initial_state, dfinal and dinitial may be
+ * null (zeros / not written). Chunks run in parallel: the forward writes each chunk's state
+ * contribution into chunk_states and scans them (in place) into the chunk-start states; the
+ * backward scans the chunk gradients in reverse in its workspace. The bias, rotation, scale, D skip, gate and rank sum around the core are left to the
  * caller's autograd.
  */
 typedef struct m3_ssd_args {
@@ -211,10 +213,15 @@ typedef struct m3_ssd_args {
   m3_tensor y, final_state, chunk_states;
   m3_tensor dy, dfinal;
   m3_tensor dq, dk, dv, dadt, ddiag, dinitial;
+  m3_tensor workspace; /* float32, 16-byte aligned, m3_ssd_workspace_bytes(args, backward) bytes */
 } m3_ssd_args;
 
 /* Rows (token, rank) per chunk of the training kernels. */
 int m3_ssd_chunk_rows(void);
+
+/* Bytes of float32 scratch the training forward (backward = 0) or backward (1) needs; negative:
+ * minus an M3_ERR_* code. */
+int64_t m3_ssd_workspace_bytes(const m3_ssd_args* args, int backward);
 
 /* Forward of the SSD core for training: y, final_state and chunk_states. M3_OK or M3_ERR_*. */
 int m3_ssd_train_fwd(const m3_ssd_args* args, void* stream);

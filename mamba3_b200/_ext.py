@@ -77,6 +77,7 @@ _SSD_TENSORS = (
     "y", "final_state", "chunk_states",
     "dy", "dfinal",
     "dq", "dk", "dv", "dadt", "ddiag", "dinitial",
+    "workspace",
 )
 
 
@@ -134,6 +135,8 @@ def load() -> ctypes.CDLL:
         lib.m3_last_step_kernel.restype = ctypes.c_char_p
         lib.m3_ssd_chunk_rows.argtypes = []
         lib.m3_ssd_chunk_rows.restype = ctypes.c_int
+        lib.m3_ssd_workspace_bytes.argtypes = [ctypes.POINTER(SSDArgs), ctypes.c_int]
+        lib.m3_ssd_workspace_bytes.restype = ctypes.c_int64
         lib.m3_ssd_train_fwd.argtypes = [ctypes.POINTER(SSDArgs), ctypes.c_void_p]
         lib.m3_ssd_train_fwd.restype = ctypes.c_int
         lib.m3_ssd_train_bwd.argtypes = [ctypes.POINTER(SSDArgs), ctypes.c_void_p]
@@ -334,7 +337,9 @@ def scan_forward_noalloc(*, sizes: dict, tensors: dict, reverse: bool = False, m
     _check(lib.m3_scan_fwd_noalloc(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
 
 
-def _ssd_args(q: torch.Tensor, tensors: dict) -> SSDArgs:
+def _ssd_args(q: torch.Tensor, tensors: dict, backward: bool) -> SSDArgs:
+    """Argument struct of the training kernels, with the scratch they need allocated on q's device."""
+    lib = load()
     batch, length, heads, rank, d_state = q.shape
     args = SSDArgs()
     args.batch, args.length, args.heads, args.rank, args.d_state = batch, length, heads, rank, d_state
@@ -342,6 +347,12 @@ def _ssd_args(q: torch.Tensor, tensors: dict) -> SSDArgs:
     args.device = q.device.index if q.device.index is not None else torch.cuda.current_device()
     for name in _SSD_TENSORS:
         setattr(args, name, _desc(tensors.get(name)))
+    need = lib.m3_ssd_workspace_bytes(ctypes.byref(args), int(backward))
+    if need < 0:
+        _check(int(-need), lib)
+    workspace = torch.empty((need + 3) // 4, device=q.device, dtype=torch.float32)
+    args.workspace = _desc(workspace)
+    args._keep = workspace  # alive until the launch is enqueued (stream-ordered reuse after that)
     return args
 
 
@@ -360,7 +371,7 @@ def ssd_train_forward(q, k, v, adt, diag, initial_state):
     final = torch.empty(batch, heads, head_dim, d_state, device=dev, dtype=torch.float32)
     chunks = torch.empty(batch, heads, nchunk, head_dim, d_state, device=dev, dtype=torch.float32)
     args = _ssd_args(q, dict(q=q, k=k, v=v, adt=adt, diag=diag, initial_state=initial_state, y=y,
-                             final_state=final, chunk_states=chunks))
+                             final_state=final, chunk_states=chunks), backward=False)
     stream = torch.cuda.current_stream(dev).cuda_stream
     _check(lib.m3_ssd_train_fwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
     return y, final, chunks
@@ -381,7 +392,7 @@ def ssd_train_backward(q, k, v, adt, diag, chunk_states, dy, dfinal, want_initia
     dinit = (torch.empty(batch, heads, head_dim, d_state, device=dev, dtype=torch.float32)
              if want_initial else None)
     args = _ssd_args(q, dict(q=q, k=k, v=v, adt=adt, diag=diag, chunk_states=chunk_states, dy=dy, dfinal=dfinal,
-                             dq=dq, dk=dk, dv=dv, dadt=dadt, ddiag=ddiag, dinitial=dinit))
+                             dq=dq, dk=dk, dv=dv, dadt=dadt, ddiag=ddiag, dinitial=dinit), backward=True)
     stream = torch.cuda.current_stream(dev).cuda_stream
     _check(lib.m3_ssd_train_bwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
     return dq, dk, dv, dadt, ddiag, dinit

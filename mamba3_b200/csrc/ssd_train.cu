@@ -10,15 +10,24 @@
 // q, k (k already times the trapezoid scale), v (rank values) are float32 here; the bias, rotation,
 // scale, D skip, SiLU gate and rank sum around the core stay differentiable PyTorch ops.
 //
-// Backward, chunks in reverse with dS = dLoss/dS_{c+1} resident in shared memory:
+// Backward, with G_c = dLoss/dS_{c+1} (the gradient of chunk c's end state):
 //   dq_i = e^{cum_t} S_c^T dy_i + sum_j M_ij k_j,        M_ij = L_ts (dy_i . v_j)
-//   dk_j = T_s dS^T v_j + sum_i M_ij q_i,                T_s = e^{cum_last - cum_s}
-//   dv_j = T_s dS k_j + sum_i Wt_ij dy_i
-//   dS_c = e^{cum_last} dS + sum_i e^{cum_t} dy_i q_i^T
+//   dk_j = T_s G_c^T v_j + sum_i M_ij q_i,               T_s = e^{cum_last - cum_s}
+//   dv_j = T_s G_c k_j + sum_i Wt_ij dy_i
+//   dS_c = e^{cum_last} G_c + sum_i e^{cum_t} dy_i q_i^T  (= G_{c-1})
 //   dcum_t: e^{cum_t} dy_i . (S_c q_i); +- L_ts (q_i . k_j)(dy_i . v_j) for s < t;
-//           e^{cum_last} <dS, S_c> + T_s v_j . (dS k_j) on the last token, - T_s v_j . (dS k_j) on s
+//           e^{cum_last} <G_c, S_c> + T_s v_j . (G_c k_j) on the last token, - T_s v_j . (G_c k_j) on s
 //   ddiag_t = sum over same-token pairs (q_i . k_j)(dy_i . v_j);  dadt = reverse cumsum of dcum.
-// One CTA (256 threads) per (batch, head); FP32 CUDA-core arithmetic from shared memory.
+//
+// Chunk-parallel schedule (only the two carries are sequential, as elementwise scans):
+//   forward:  chunk_delta (per chunk: sum_j T_s v_j k_j^T and e^{cum_last})
+//             -> state_scan (per (batch, head): S_{c+1} = e^{cum_last} S_c + delta_c, S_c kept)
+//             -> chunk_output (per chunk: y)
+//   backward: chunk_delta (per chunk: sum_i e^{cum_t} dy_i q_i^T)
+//             -> grad_scan (per (batch, head), reverse: G_c kept, <G_c, S_c>)
+//             -> chunk_grads (per chunk: dq, dk, dv, dadt, ddiag)
+// Per-chunk kernels: one CTA (256 threads) per (chunk, head, batch), FP32 CUDA-core products from
+// shared memory, each thread accumulating a register tile with 128-bit shared loads.
 #include <string>
 
 #include "common.cuh"
@@ -26,69 +35,40 @@
 namespace m3 {
 namespace ssdt {
 
-constexpr int kRows = 32;      // rows per chunk
+constexpr int kRows = 32;  // rows per chunk
 constexpr int kThreads = 256;
 constexpr int kMaxN = 128, kMaxP = 64;
 
-struct Smem {
-  int N, P;
-  int ldn, ldp;  // padded row strides (N + 1, P + 1): conflict-free column walks
-  float *S, *dS, *Q, *K, *V, *dY, *A, *W, *M, *red;
-};
-
-__host__ __device__ inline size_t smem_floats(int N, int P, bool bwd) {
-  const size_t st = (size_t)P * (N + 1);
-  const size_t rows = (size_t)kRows * (N + 1) * 2 + (size_t)kRows * (P + 1) * 2;
-  const size_t sq = (size_t)kRows * (kRows + 1) * 3;
-  return st * (bwd ? 2 : 1) + rows + sq + 6 * kRows;  // red: cum, e^cum, T, dcum, ddiag, scalars
+// Offset of row (t, r) of a [B, L, H, R, X] tensor.
+__device__ __forceinline__ int64_t row_off(const m3_tensor& t, int b, int tok, int h, int r) {
+  return b * t.stride[0] + (int64_t)tok * t.stride[1] + h * t.stride[2] + r * t.stride[3];
 }
 
-__device__ inline Smem carve(float* base, int N, int P, bool bwd) {
-  Smem s;
-  s.N = N, s.P = P, s.ldn = N + 1, s.ldp = P + 1;
-  float* p = base;
-  s.S = p, p += (size_t)P * s.ldn;
-  s.dS = bwd ? p : nullptr;
-  if (bwd) p += (size_t)P * s.ldn;
-  s.Q = p, p += kRows * s.ldn;
-  s.K = p, p += kRows * s.ldn;
-  s.V = p, p += kRows * s.ldp;
-  s.dY = p, p += kRows * s.ldp;
-  s.A = p, p += kRows * (kRows + 1);
-  s.W = p, p += kRows * (kRows + 1);
-  s.M = p, p += kRows * (kRows + 1);
-  s.red = p;  // [6][kRows]: cum, e^{cum}, T, dcum, ddiag, scalars
-  return s;
-}
-
-// Row (t, r) of a [B, L, H, R, X] tensor.
-__device__ __forceinline__ const float* row_ptr(const m3_tensor& t, int b, int tok, int h, int r) {
-  return static_cast<const float*>(t.data) + b * t.stride[0] + (int64_t)tok * t.stride[1] + h * t.stride[2] +
-         r * t.stride[3];
-}
-__device__ __forceinline__ float* row_ptr_w(const m3_tensor& t, int b, int tok, int h, int r) {
-  return static_cast<float*>(t.data) + b * t.stride[0] + (int64_t)tok * t.stride[1] + h * t.stride[2] +
-         r * t.stride[3];
-}
-
-// Loads the chunk's rows [row0, row0 + rows) of a [B, L, H, R, X] tensor into dst [kRows][ld]
-// (rows past the end zero).
+// Loads rows [row0, row0 + rows) (flattened (token, rank)) of a [B, L, H, R, X] float tensor with
+// contiguous, 16-byte aligned rows into dst [kRows][ld], scaled per row by scale[row / R] when given;
+// rows past `rows` are zero. One warp per row, 16-byte loads (X <= 128).
 __device__ inline void load_rows(float* dst, int ld, const m3_tensor& t, int b, int h, int R, int row0, int rows,
-                                 int X) {
-  for (int o = threadIdx.x; o < kRows * X; o += kThreads) {
-    const int i = o / X, x = o % X;
-    float v = 0.0f;
+                                 int X, const float* scale = nullptr) {
+  const float* base = static_cast<const float*>(t.data);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = warp; i < kRows; i += kThreads / 32) {
+    if (4 * lane >= X) continue;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (i < rows) {
       const int row = row0 + i;
-      v = row_ptr(t, b, row / R, h, row % R)[x * t.stride[4]];
+      v = *reinterpret_cast<const float4*>(base + row_off(t, b, row / R, h, row % R) + 4 * lane);
+      if (scale) {
+        const float f = scale[i / R];
+        v.x *= f, v.y *= f, v.z *= f, v.w *= f;
+      }
     }
-    dst[i * ld + x] = v;
+    *reinterpret_cast<float4*>(dst + i * ld + 4 * lane) = v;
   }
 }
 
-// Per-token scalars of the chunk (warp 0): cum (inclusive), e^{cum}, e^{cum_last - cum}; returns
-// nothing, fills red[0..2][token].
-__device__ inline void chunk_scalars(const Smem& s, const m3_tensor& adt, int b, int h, int t0, int ntok) {
+// Per-token scalars of a chunk (warp 0): red[0..] cum, red[32..] e^{cum}, red[64..] e^{cum_last - cum}
+// (zero past the sequence end).
+__device__ inline void chunk_scalars(float* red, const m3_tensor& adt, int b, int h, int t0, int ntok) {
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     const float a = lane < ntok ? static_cast<const float*>(adt.data)[b * adt.stride[0] + (int64_t)(t0 + lane) *
@@ -96,266 +76,541 @@ __device__ inline void chunk_scalars(const Smem& s, const m3_tensor& adt, int b,
                                 : 0.0f;
     const float cum = warp_incl_scan(a, lane);
     const float last = __shfl_sync(0xffffffffu, cum, max(ntok - 1, 0));
-    s.red[lane] = cum;
-    s.red[kRows + lane] = lane < ntok ? expf(cum) : 0.0f;
-    s.red[2 * kRows + lane] = lane < ntok ? expf(last - cum) : 0.0f;
+    red[lane] = cum;
+    red[kRows + lane] = lane < ntok ? expf(cum) : 0.0f;
+    red[2 * kRows + lane] = lane < ntok ? expf(last - cum) : 0.0f;
   }
 }
 
-__device__ __forceinline__ float diag_of(const m3_tensor& d, int b, int t, int h) {
-  return static_cast<const float*>(d.data)[b * d.stride[0] + (int64_t)t * d.stride[1] + h * d.stride[2]];
-}
-
-// Lower-triangular token weights L_ts (including diag_t on s == t).
-__device__ __forceinline__ float lweight(const Smem& s, int t, int u, float dg) {
-  return u < t ? expf(s.red[t] - s.red[u]) : (u == t ? dg : 0.0f);
-}
-
-__global__ void __launch_bounds__(kThreads) ssd_fwd_kernel(const m3_ssd_args a) {
-  extern __shared__ float smem[];
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-  const int N = a.d_state, P = a.head_dim, R = a.rank, L = a.length;
-  const Smem s = carve(smem, N, P, false);
-  const int tok_per = kRows / R;
-  const int nchunk = (L + tok_per - 1) / tok_per;
-  // initial state
-  for (int o = tid; o < P * N; o += kThreads) {
-    const int p = o / N, n = o % N;
-    float v = 0.0f;
-    if (a.initial_state.data) {
-      const m3_tensor& t = a.initial_state;
-      v = static_cast<const float*>(t.data)[b * t.stride[0] + h * t.stride[1] + p * t.stride[2] + n * t.stride[3]];
-    }
-    s.S[p * s.ldn + n] = v;
-  }
-  for (int c = 0; c < nchunk; ++c) {
-    const int t0 = c * tok_per, ntok = min(tok_per, L - t0), rows = ntok * R;
-    __syncthreads();
-    // keep S_c for the backward
-    {
-      const m3_tensor& cs = a.chunk_states;
-      float* dst = static_cast<float*>(cs.data) + b * cs.stride[0] + h * cs.stride[1] + (int64_t)c * cs.stride[2];
-      for (int o = tid; o < P * N; o += kThreads) {
-        const int p = o / N, n = o % N;
-        dst[p * cs.stride[3] + n * cs.stride[4]] = s.S[p * s.ldn + n];
-      }
-    }
-    load_rows(s.Q, s.ldn, a.q, b, h, R, t0 * R, rows, N);
-    load_rows(s.K, s.ldn, a.k, b, h, R, t0 * R, rows, N);
-    load_rows(s.V, s.ldp, a.v, b, h, R, t0 * R, rows, P);
-    chunk_scalars(s, a.adt, b, h, t0, ntok);
-    __syncthreads();
-    // Wt = L o (Q K^T)
-    for (int o = tid; o < kRows * kRows; o += kThreads) {
-      const int i = o / kRows, j = o % kRows;
-      float w = 0.0f;
-      if (i < rows && j < rows) {
-        const int ti = i / R, tj = j / R;
-        const float lw = lweight(s, ti, tj, tj == ti ? diag_of(a.diag, b, t0 + ti, h) : 0.0f);
-        if (lw != 0.0f) {
-          float acc = 0.0f;
-          for (int n = 0; n < N; ++n) acc = fmaf(s.Q[i * s.ldn + n], s.K[j * s.ldn + n], acc);
-          w = lw * acc;
-        }
-      }
-      s.W[i * (kRows + 1) + j] = w;
-    }
-    __syncthreads();
-    // y_i = e^{cum_t} S_c q_i + sum_j Wt_ij v_j
-    for (int o = tid; o < rows * P; o += kThreads) {
-      const int i = o / P, p = o % P;
-      float inter = 0.0f;
-      for (int n = 0; n < N; ++n) inter = fmaf(s.S[p * s.ldn + n], s.Q[i * s.ldn + n], inter);
-      float intra = 0.0f;
-      for (int j = 0; j <= min(rows - 1, (i / R + 1) * R - 1); ++j)
-        intra = fmaf(s.W[i * (kRows + 1) + j], s.V[j * s.ldp + p], intra);
-      const int row = t0 * R + i;
-      row_ptr_w(a.y, b, row / R, h, row % R)[p * a.y.stride[4]] = s.red[kRows + i / R] * inter + intra;
-    }
-    __syncthreads();
-    // S_{c+1} = e^{cum_last} S_c + sum_j T_s v_j k_j^T
-    const float lam = expf(s.red[ntok - 1]);
-    for (int o = tid; o < P * N; o += kThreads) {
-      const int p = o / N, n = o % N;
-      float acc = 0.0f;
-      for (int j = 0; j < rows; ++j) acc = fmaf(s.red[2 * kRows + j / R] * s.V[j * s.ldp + p], s.K[j * s.ldn + n], acc);
-      s.S[p * s.ldn + n] = fmaf(lam, s.S[p * s.ldn + n], acc);
-    }
-  }
-  __syncthreads();
-  const m3_tensor& fs = a.final_state;
-  for (int o = tid; o < P * N; o += kThreads) {
-    const int p = o / N, n = o % N;
-    static_cast<float*>(fs.data)[b * fs.stride[0] + h * fs.stride[1] + p * fs.stride[2] + n * fs.stride[3]] =
-        s.S[p * s.ldn + n];
-  }
-}
-
-__global__ void __launch_bounds__(kThreads) ssd_bwd_kernel(const m3_ssd_args a) {
-  extern __shared__ float smem[];
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int N = a.d_state, P = a.head_dim, R = a.rank, L = a.length;
-  const Smem s = carve(smem, N, P, true);
-  const int tok_per = kRows / R;
-  const int nchunk = (L + tok_per - 1) / tok_per;
-  float* dcum = s.red + 3 * kRows;     // [kRows] per token
-  float* ddg = s.red + 4 * kRows;      // [kRows] per token (diag gradient)
-  float* scal = s.red + 5 * kRows;     // [0]: <dS, S_c>
-  // dS = gradient of the final state
-  for (int o = tid; o < P * N; o += kThreads) {
-    const int p = o / N, n = o % N;
-    float v = 0.0f;
-    if (a.dfinal.data) {
-      const m3_tensor& t = a.dfinal;
-      v = static_cast<const float*>(t.data)[b * t.stride[0] + h * t.stride[1] + p * t.stride[2] + n * t.stride[3]];
-    }
-    s.dS[p * s.ldn + n] = v;
-  }
-  for (int c = nchunk - 1; c >= 0; --c) {
-    const int t0 = c * tok_per, ntok = min(tok_per, L - t0), rows = ntok * R;
-    __syncthreads();
-    {
-      const m3_tensor& cs = a.chunk_states;
-      const float* src = static_cast<const float*>(cs.data) + b * cs.stride[0] + h * cs.stride[1] +
-                         (int64_t)c * cs.stride[2];
-      for (int o = tid; o < P * N; o += kThreads) {
-        const int p = o / N, n = o % N;
-        s.S[p * s.ldn + n] = src[p * cs.stride[3] + n * cs.stride[4]];
-      }
-    }
-    load_rows(s.Q, s.ldn, a.q, b, h, R, t0 * R, rows, N);
-    load_rows(s.K, s.ldn, a.k, b, h, R, t0 * R, rows, N);
-    load_rows(s.V, s.ldp, a.v, b, h, R, t0 * R, rows, P);
-    load_rows(s.dY, s.ldp, a.dy, b, h, R, t0 * R, rows, P);
-    chunk_scalars(s, a.adt, b, h, t0, ntok);
-    if (tid < kRows) dcum[tid] = ddg[tid] = 0.0f;
-    if (tid == 0) scal[0] = 0.0f;
-    __syncthreads();
-    // A = Q K^T, B = dY V^T; Wt = L o A, M = L o B; the decay and diagonal gradients of each pair.
-    for (int o = tid; o < kRows * kRows; o += kThreads) {
-      const int i = o / kRows, j = o % kRows;
-      float wt = 0.0f, m = 0.0f;
-      if (i < rows && j < rows && j / R <= i / R) {
-        const int ti = i / R, tj = j / R;
-        float qa = 0.0f, bb = 0.0f;
-        for (int n = 0; n < N; ++n) qa = fmaf(s.Q[i * s.ldn + n], s.K[j * s.ldn + n], qa);
-        for (int p = 0; p < P; ++p) bb = fmaf(s.dY[i * s.ldp + p], s.V[j * s.ldp + p], bb);
-        if (tj == ti) {
-          const float dg = diag_of(a.diag, b, t0 + ti, h);
-          wt = dg * qa;
-          m = dg * bb;
-          atomicAdd(&ddg[ti], qa * bb);
+// Register-tiled product: acc[TM][TN] += sum_k A(m0 + t, k) B(k, n0 + u) over k in [0, K) (K a
+// multiple of 4). A is stored k-major (A(m, k) = A[k * lda + m]) when AK, else m-major
+// (A[m * lda + k]); B likewise with BK (B(k, n) = B[k * ldb + n]) or n-major (B[n * ldb + k]).
+// Every shared load is a 16- or 8-byte vector: row starts and strides are multiples of 4 floats.
+template <int TM, int TN, bool AK, bool BK>
+__device__ __forceinline__ void mm(float (&acc)[TM][TN], const float* A, int lda, const float* B, int ldb, int K,
+                                   int m0, int n0) {
+  static_assert(TM % 2 == 0 && TN % 2 == 0, "even tiles");
+  for (int k = 0; k < K; k += 4) {
+    float a[4][TM], bb[4][TN];
+    if constexpr (AK) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float* src = A + (k + kk) * lda + m0;
+        if constexpr (TM % 4 == 0) {
+#pragma unroll
+          for (int t = 0; t < TM; t += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(src + t);
+            a[kk][t] = v.x, a[kk][t + 1] = v.y, a[kk][t + 2] = v.z, a[kk][t + 3] = v.w;
+          }
         } else {
-          const float lw = expf(s.red[ti] - s.red[tj]);
-          wt = lw * qa;
-          m = lw * bb;
-          const float g = lw * qa * bb;
-          atomicAdd(&dcum[ti], g);
-          atomicAdd(&dcum[tj], -g);
+#pragma unroll
+          for (int t = 0; t < TM; t += 2) {
+            const float2 v = *reinterpret_cast<const float2*>(src + t);
+            a[kk][t] = v.x, a[kk][t + 1] = v.y;
+          }
         }
       }
-      s.W[i * (kRows + 1) + j] = wt;
-      s.M[i * (kRows + 1) + j] = m;
+    } else {
+#pragma unroll
+      for (int t = 0; t < TM; ++t) {
+        const float4 v = *reinterpret_cast<const float4*>(A + (m0 + t) * lda + k);
+        a[0][t] = v.x, a[1][t] = v.y, a[2][t] = v.z, a[3][t] = v.w;
+      }
     }
-    // <dS, S_c> (for the e^{cum_last} factor of the carried state)
-    {
-      float acc = 0.0f;
-      for (int o = tid; o < P * N; o += kThreads) {
-        const int p = o / N, n = o % N;
-        acc = fmaf(s.dS[p * s.ldn + n], s.S[p * s.ldn + n], acc);
+    if constexpr (BK) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float* src = B + (k + kk) * ldb + n0;
+        if constexpr (TN % 4 == 0) {
+#pragma unroll
+          for (int u = 0; u < TN; u += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(src + u);
+            bb[kk][u] = v.x, bb[kk][u + 1] = v.y, bb[kk][u + 2] = v.z, bb[kk][u + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < TN; u += 2) {
+            const float2 v = *reinterpret_cast<const float2*>(src + u);
+            bb[kk][u] = v.x, bb[kk][u + 1] = v.y;
+          }
+        }
       }
-      acc = warp_sum(acc);
-      if (lane == 0) atomicAdd(&scal[0], acc);
+    } else {
+#pragma unroll
+      for (int u = 0; u < TN; ++u) {
+        const float4 v = *reinterpret_cast<const float4*>(B + (n0 + u) * ldb + k);
+        bb[0][u] = v.x, bb[1][u] = v.y, bb[2][u] = v.z, bb[3][u] = v.w;
+      }
     }
-    __syncthreads();
-    // dq_i = e^{cum_t} S_c^T dy_i + sum_j M_ij k_j ; dk_j = T_s dS^T v_j + sum_i M_ij q_i
-    for (int o = tid; o < rows * N; o += kThreads) {
-      const int i = o / N, n = o % N;
-      const int ti = i / R;
-      float inter = 0.0f, sv = 0.0f;
-      for (int p = 0; p < P; ++p) {
-        inter = fmaf(s.S[p * s.ldn + n], s.dY[i * s.ldp + p], inter);
-        sv = fmaf(s.dS[p * s.ldn + n], s.V[i * s.ldp + p], sv);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+      for (int t = 0; t < TM; ++t)
+#pragma unroll
+        for (int u = 0; u < TN; ++u) acc[t][u] = fmaf(a[kk][t], bb[kk][u], acc[t][u]);
+  }
+}
+
+template <int TM, int TN> __device__ __forceinline__ void zero(float (&acc)[TM][TN]) {
+#pragma unroll
+  for (int t = 0; t < TM; ++t)
+#pragma unroll
+    for (int u = 0; u < TN; ++u) acc[t][u] = 0.0f;
+}
+
+// Padded shared row strides (multiples of 4 floats; the +4 staggers rows across banks).
+__host__ __device__ constexpr int ldn(int N) { return N + 4; }
+__host__ __device__ constexpr int ldp(int P) { return P + 4; }
+constexpr int kLdr = kRows + 4;
+
+struct Geo {
+  int N, P, R, L, tok_per, nchunk;
+};
+__device__ __forceinline__ Geo geo(const m3_ssd_args& a) {
+  Geo g;
+  g.N = a.d_state, g.P = a.head_dim, g.R = a.rank, g.L = a.length;
+  g.tok_per = kRows / g.R;
+  g.nchunk = (g.L + g.tok_per - 1) / g.tok_per;
+  return g;
+}
+
+// Chunk-state buffer [B][H][nchunk][P][N] (contiguous).
+__device__ __forceinline__ float* chunk_slot(const m3_ssd_args& a, const Geo& g, int b, int h, int c) {
+  return static_cast<float*>(a.chunk_states.data) + (((int64_t)b * a.heads + h) * g.nchunk + c) * g.P * g.N;
+}
+
+__device__ __forceinline__ float diag_at(const m3_ssd_args& a, int b, int t, int h) {
+  return static_cast<const float*>(a.diag.data)[b * a.diag.stride[0] + (int64_t)t * a.diag.stride[1] +
+                                                h * a.diag.stride[2]];
+}
+
+// delta_c = sum_j w_j x_j y_j^T over the chunk rows ([P][N]) into `out`, with x = v (w = T_s) for the
+// forward or x = dy (w = e^{cum_t}) for the backward, y = k or q. Also writes e^{cum_last} to lam.
+__global__ void __launch_bounds__(kThreads) chunk_delta_kernel(const m3_ssd_args a, int bwd, float* out, float* lam) {
+  extern __shared__ float smem[];
+  const Geo g = geo(a);
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int t0 = c * g.tok_per, ntok = min(g.tok_per, g.L - t0), rows = ntok * g.R;
+  float* X = smem;                    // [kRows][ldp]
+  float* Y = X + kRows * ldp(g.P);    // [kRows][ldn]
+  float* red = Y + kRows * ldn(g.N);  // [3][kRows]
+  chunk_scalars(red, a.adt, b, h, t0, ntok);
+  __syncthreads();
+  load_rows(X, ldp(g.P), bwd ? a.dy : a.v, b, h, g.R, t0 * g.R, rows, g.P, red + (bwd ? kRows : 2 * kRows));
+  load_rows(Y, ldn(g.N), bwd ? a.q : a.k, b, h, g.R, t0 * g.R, rows, g.N);
+  __syncthreads();
+  float* dst = out + (((int64_t)b * a.heads + h) * g.nchunk + c) * g.P * g.N;
+  const int tiles_n = g.N / 8;
+  for (int tile = threadIdx.x; tile < (g.P / 4) * tiles_n; tile += kThreads) {
+    const int m0 = (tile / tiles_n) * 4, n0 = (tile % tiles_n) * 8;
+    float acc[4][8];
+    zero(acc);
+    mm<4, 8, true, true>(acc, X, ldp(g.P), Y, ldn(g.N), kRows, m0, n0);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      float4* d = reinterpret_cast<float4*>(dst + (m0 + t) * g.N + n0);
+      d[0] = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
+      d[1] = make_float4(acc[t][4], acc[t][5], acc[t][6], acc[t][7]);
+    }
+  }
+  if (threadIdx.x == 0) lam[((int64_t)b * a.heads + h) * g.nchunk + c] = expf(red[ntok - 1]);
+}
+
+// Forward carry, per (batch, head): slot c holds delta_c on entry and S_c on exit;
+// S_{c+1} = lam_c S_c + delta_c; the last S is the final state. Thread: float4 groups
+// e = 4 (tid + 256 q); the next chunk's deltas are loaded before the current chunk is stored.
+constexpr int kMaxPer = kMaxN * kMaxP / (kThreads * 4);  // float4 groups per thread
+
+__global__ void __launch_bounds__(kThreads) state_scan_kernel(const m3_ssd_args a, const float* lam) {
+  const Geo g = geo(a);
+  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int PN = g.P * g.N;
+  const float* lp = lam + ((int64_t)b * a.heads + h) * g.nchunk;
+  float4 s[kMaxPer], d[kMaxPer];
+#pragma unroll
+  for (int q = 0; q < kMaxPer; ++q) {
+    const int e = (tid + q * kThreads) * 4;
+    s[q] = d[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e < PN) {
+      if (a.initial_state.data) {
+        const int p = e / g.N, n = e % g.N;
+        const m3_tensor& t = a.initial_state;
+        const float* src = static_cast<const float*>(t.data) + b * t.stride[0] + h * t.stride[1] + p * t.stride[2];
+        s[q] = make_float4(src[n * t.stride[3]], src[(n + 1) * t.stride[3]], src[(n + 2) * t.stride[3]],
+                           src[(n + 3) * t.stride[3]]);
       }
-      float dq = s.red[kRows + ti] * inter, dk = s.red[2 * kRows + ti] * sv;
-      for (int j = 0; j < rows; ++j) {
-        dq = fmaf(s.M[i * (kRows + 1) + j], s.K[j * s.ldn + n], dq);  // M_ij (zero above the token)
-        dk = fmaf(s.M[j * (kRows + 1) + i], s.Q[j * s.ldn + n], dk);  // M_ji: rows j at or after i
+      d[q] = *reinterpret_cast<const float4*>(chunk_slot(a, g, b, h, 0) + e);
+    }
+  }
+  for (int c = 0; c < g.nchunk; ++c) {
+    float4 nx[kMaxPer];
+    float* slot = chunk_slot(a, g, b, h, c);
+    const bool more = c + 1 < g.nchunk;
+    const float* next = more ? chunk_slot(a, g, b, h, c + 1) : slot;
+    const float l = lp[c];
+#pragma unroll
+    for (int q = 0; q < kMaxPer; ++q) {
+      const int e = (tid + q * kThreads) * 4;
+      nx[q] = (e < PN && more) ? *reinterpret_cast<const float4*>(next + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int q = 0; q < kMaxPer; ++q) {
+      const int e = (tid + q * kThreads) * 4;
+      if (e < PN) {
+        *reinterpret_cast<float4*>(slot + e) = s[q];
+        s[q] = make_float4(fmaf(l, s[q].x, d[q].x), fmaf(l, s[q].y, d[q].y), fmaf(l, s[q].z, d[q].z),
+                           fmaf(l, s[q].w, d[q].w));
+        d[q] = nx[q];
       }
+    }
+  }
+  const m3_tensor& f = a.final_state;
+#pragma unroll
+  for (int q = 0; q < kMaxPer; ++q) {
+    const int e = (tid + q * kThreads) * 4;
+    if (e < PN) {
+      const int p = e / g.N, n = e % g.N;
+      float* dst = static_cast<float*>(f.data) + b * f.stride[0] + h * f.stride[1] + p * f.stride[2];
+      dst[n * f.stride[3]] = s[q].x, dst[(n + 1) * f.stride[3]] = s[q].y;
+      dst[(n + 2) * f.stride[3]] = s[q].z, dst[(n + 3) * f.stride[3]] = s[q].w;
+    }
+  }
+}
+
+// y_i = e^{cum_t} S_c q_i + sum_j Wt_ij v_j per chunk.
+__global__ void __launch_bounds__(kThreads) chunk_output_kernel(const m3_ssd_args a) {
+  extern __shared__ float smem[];
+  const Geo g = geo(a);
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int t0 = c * g.tok_per, ntok = min(g.tok_per, g.L - t0), rows = ntok * g.R, R = g.R;
+  const int LN = ldn(g.N), LP = ldp(g.P);
+  float* S = smem;                // [P][LN]
+  float* Q = S + g.P * LN;        // [kRows][LN]
+  float* K = Q + kRows * LN;      // [kRows][LN]
+  float* V = K + kRows * LN;      // [kRows][LP]
+  float* W = V + kRows * LP;      // [kRows][kLdr]
+  float* red = W + kRows * kLdr;  // [3][kRows]
+  chunk_scalars(red, a.adt, b, h, t0, ntok);
+  {
+    const float* src = chunk_slot(a, g, b, h, c);
+    for (int e = tid * 4; e < g.P * g.N; e += kThreads * 4)
+      *reinterpret_cast<float4*>(S + (e / g.N) * LN + e % g.N) = *reinterpret_cast<const float4*>(src + e);
+  }
+  load_rows(Q, LN, a.q, b, h, R, t0 * R, rows, g.N);
+  load_rows(K, LN, a.k, b, h, R, t0 * R, rows, g.N);
+  load_rows(V, LP, a.v, b, h, R, t0 * R, rows, g.P);
+  __syncthreads();
+  // Wt = L o (Q K^T): 2 x 2 tiles
+  {
+    const int m0 = (tid / 16) * 2, n0 = (tid % 16) * 2;
+    float acc[2][2];
+    zero(acc);
+    mm<2, 2, false, false>(acc, Q, LN, K, LN, g.N, m0, n0);
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = m0 + t, j = n0 + u, ti = i / R, tj = j / R;
+        float w = 0.0f;
+        if (i < rows && j < rows && tj <= ti)
+          w = (tj < ti ? expf(red[ti] - red[tj]) : diag_at(a, b, t0 + ti, h)) * acc[t][u];
+        W[i * kLdr + j] = w;
+      }
+  }
+  __syncthreads();
+  // y = e^{cum} (Q S^T) + W V: 2 x 4 tiles over [kRows][P]
+  const int tiles_n = g.P / 4;
+  for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
+    const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 4;
+    float inter[2][4], intra[2][4];
+    zero(inter);
+    zero(intra);
+    mm<2, 4, false, false>(inter, Q, LN, S, LN, g.N, m0, n0);
+    mm<2, 4, false, true>(intra, W, kLdr, V, LP, kRows, m0, n0);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int i = m0 + t;
+      if (i >= rows) continue;
       const int row = t0 * R + i;
-      row_ptr_w(a.dq, b, row / R, h, row % R)[n * a.dq.stride[4]] = dq;
-      row_ptr_w(a.dk, b, row / R, h, row % R)[n * a.dk.stride[4]] = dk;
+      float* dst = static_cast<float*>(a.y.data) + row_off(a.y, b, row / R, h, row % R);
+      const float e = red[kRows + i / R];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) dst[(n0 + u) * a.y.stride[4]] = fmaf(e, inter[t][u], intra[t][u]);
     }
-    // dv_j = T_s dS k_j + sum_i Wt_ij dy_i ; dcum from the state term (v_j . dS k_j) and the inter
-    // term (dy_i . S_c q_i)
-    for (int o = tid; o < kRows * P; o += kThreads) {
-      const int j = o / P, p = o % P;
-      float dv = 0.0f, sdot = 0.0f, idot = 0.0f;
-      if (j < rows) {
-        const int tj = j / R;
-        float dsk = 0.0f, sq = 0.0f;
-        for (int n = 0; n < N; ++n) {
-          dsk = fmaf(s.dS[p * s.ldn + n], s.K[j * s.ldn + n], dsk);
-          sq = fmaf(s.S[p * s.ldn + n], s.Q[j * s.ldn + n], sq);
-        }
-        const float T = s.red[2 * kRows + tj];
-        dv = T * dsk;
-        for (int i = tj * R; i < rows; ++i) dv = fmaf(s.W[i * (kRows + 1) + j], s.dY[i * s.ldp + p], dv);
-        sdot = T * s.V[j * s.ldp + p] * dsk;
-        idot = s.red[kRows + tj] * s.dY[j * s.ldp + p] * sq;
-        const int row = t0 * R + j;
-        row_ptr_w(a.dv, b, row / R, h, row % R)[p * a.dv.stride[4]] = dv;
+  }
+}
+
+// Backward carry, per (batch, head), chunks in reverse: slot c holds sum_i e^{cum_t} dy_i q_i^T on
+// entry and G_c = dLoss/dS_{c+1} on exit; dS_c = lam_c G_c + delta_c. Also <G_c, S_c> per chunk
+// (into gs) and the gradient of the initial state.
+__global__ void __launch_bounds__(kThreads) grad_scan_kernel(const m3_ssd_args a, float* grads, const float* lam,
+                                                             float* gs) {
+  const Geo g = geo(a);
+  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int PN = g.P * g.N;
+  const int64_t base = ((int64_t)b * a.heads + h) * g.nchunk;
+  __shared__ float part[kThreads / 32];
+  float4 d[kMaxPer], dl[kMaxPer], st4[kMaxPer];  // carry; this chunk's delta and S_c
+#pragma unroll
+  for (int q = 0; q < kMaxPer; ++q) {
+    const int e = (tid + q * kThreads) * 4;
+    d[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e < PN && a.dfinal.data) {
+      const int p = e / g.N, n = e % g.N;
+      const m3_tensor& t = a.dfinal;
+      const float* src = static_cast<const float*>(t.data) + b * t.stride[0] + h * t.stride[1] + p * t.stride[2];
+      d[q] = make_float4(src[n * t.stride[3]], src[(n + 1) * t.stride[3]], src[(n + 2) * t.stride[3]],
+                         src[(n + 3) * t.stride[3]]);
+    }
+  }
+  auto fetch = [&](int c, float4* dlt, float4* stc) {
+    const float* slot = grads + (base + c) * PN;
+    const float* st = chunk_slot(a, g, b, h, c);
+#pragma unroll
+    for (int q = 0; q < kMaxPer; ++q) {
+      const int e = (tid + q * kThreads) * 4;
+      dlt[q] = stc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < PN) {
+        dlt[q] = *reinterpret_cast<const float4*>(slot + e);
+        stc[q] = *reinterpret_cast<const float4*>(st + e);
       }
-      // rows j of one warp share j when P >= 32 (P a multiple of 32): reduce over the warp's p
-      const float contrib = idot - sdot;  // on token tj
-      const float last = sdot;            // on the last token
-      if (P % 32 == 0) {
-        const float c1 = warp_sum(contrib), c2 = warp_sum(last);
-        if (lane == 0 && j < rows) {
-          atomicAdd(&dcum[j / R], c1);
-          atomicAdd(&dcum[ntok - 1], c2);
-        }
-      } else if (j < rows) {
-        atomicAdd(&dcum[j / R], contrib);
-        atomicAdd(&dcum[ntok - 1], last);
+    }
+  };
+  fetch(g.nchunk - 1, dl, st4);
+  for (int c = g.nchunk - 1; c >= 0; --c) {
+    float dot = 0.0f;
+    const float l = lam[base + c];
+    float* slot = grads + (base + c) * PN;
+    float4 ndl[kMaxPer], nst[kMaxPer];
+    if (c > 0) fetch(c - 1, ndl, nst);
+#pragma unroll
+    for (int q = 0; q < kMaxPer; ++q) {
+      const int e = (tid + q * kThreads) * 4;
+      if (e < PN) {
+        *reinterpret_cast<float4*>(slot + e) = d[q];
+        const float4 s = st4[q], delta = dl[q];
+        dot += d[q].x * s.x + d[q].y * s.y + d[q].z * s.z + d[q].w * s.w;
+        d[q] = make_float4(fmaf(l, d[q].x, delta.x), fmaf(l, d[q].y, delta.y), fmaf(l, d[q].z, delta.z),
+                           fmaf(l, d[q].w, delta.w));
       }
+      if (c > 0) dl[q] = ndl[q], st4[q] = nst[q];
+    }
+    dot = warp_sum(dot);
+    if ((tid & 31) == 0) part[tid >> 5] = dot;
+    __syncthreads();
+    if (tid == 0) {
+      float s = 0.0f;
+      for (int w = 0; w < kThreads / 32; ++w) s += part[w];
+      gs[base + c] = s;
     }
     __syncthreads();
-    // dS_c = e^{cum_last} dS + sum_i e^{cum_t} dy_i q_i^T
-    const float lam = expf(s.red[ntok - 1]);
-    for (int o = tid; o < P * N; o += kThreads) {
-      const int p = o / N, n = o % N;
-      float acc = 0.0f;
-      for (int i = 0; i < rows; ++i) acc = fmaf(s.red[kRows + i / R] * s.dY[i * s.ldp + p], s.Q[i * s.ldn + n], acc);
-      s.dS[p * s.ldn + n] = fmaf(lam, s.dS[p * s.ldn + n], acc);
-    }
-    // dadt = reverse cumsum of dcum (with e^{cum_last} <dS, S_c> on the last token); ddiag
-    if (tid < 32) {
-      float v = lane < ntok ? dcum[lane] + (lane == ntok - 1 ? lam * scal[0] : 0.0f) : 0.0f;
-      // reverse inclusive scan: sum over tokens u >= lane
-      for (int off = 1; off < 32; off <<= 1) {
-        const float nb = __shfl_down_sync(0xffffffffu, v, off);
-        if (lane + off < 32) v += nb;
+  }
+  if (a.dinitial.data) {
+#pragma unroll
+    for (int q = 0; q < kMaxPer; ++q) {
+      const int e = (tid + q * kThreads) * 4;
+      if (e < PN) {
+        const int p = e / g.N, n = e % g.N;
+        const m3_tensor& t = a.dinitial;
+        float* dst = static_cast<float*>(t.data) + b * t.stride[0] + h * t.stride[1] + p * t.stride[2];
+        dst[n * t.stride[3]] = d[q].x, dst[(n + 1) * t.stride[3]] = d[q].y;
+        dst[(n + 2) * t.stride[3]] = d[q].z, dst[(n + 3) * t.stride[3]] = d[q].w;
       }
-      if (lane < ntok) {
-        const m3_tensor& da = a.dadt;
-        static_cast<float*>(da.data)[b * da.stride[0] + (int64_t)(t0 + lane) * da.stride[1] + h * da.stride[2]] = v;
-        const m3_tensor& dd = a.ddiag;
-        static_cast<float*>(dd.data)[b * dd.stride[0] + (int64_t)(t0 + lane) * dd.stride[1] + h * dd.stride[2]] =
-            ddg[lane];
+    }
+  }
+}
+
+// Per-chunk gradients. Phase 1 (S_c in shared memory): scores, Wt, M, the pair terms of dcum/ddiag,
+// dq and the inter term of dcum. Phase 2 (G_c replaces S_c): dk, dv and the state terms of dcum.
+__global__ void __launch_bounds__(kThreads) chunk_grads_kernel(const m3_ssd_args a, const float* grads,
+                                                               const float* gs) {
+  extern __shared__ float smem[];
+  const Geo g = geo(a);
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int t0 = c * g.tok_per, ntok = min(g.tok_per, g.L - t0), rows = ntok * g.R, R = g.R;
+  const int LN = ldn(g.N), LP = ldp(g.P);
+  float* S = smem;                // [P][LN]: S_c, then G_c
+  float* Q = S + g.P * LN;        // [kRows][LN]
+  float* K = Q + kRows * LN;      // [kRows][LN]
+  float* V = K + kRows * LN;      // [kRows][LP]
+  float* dY = V + kRows * LP;     // [kRows][LP]
+  float* W = dY + kRows * LP;     // [kRows][kLdr]
+  float* M = W + kRows * kLdr;    // [kRows][kLdr]
+  float* red = M + kRows * kLdr;  // cum, e^cum, T, dcum, ddiag  [5][kRows]
+  float* dcum = red + 3 * kRows;
+  float* ddg = red + 4 * kRows;
+  const int64_t bh = (int64_t)b * a.heads + h;
+  chunk_scalars(red, a.adt, b, h, t0, ntok);
+  if (tid < kRows) dcum[tid] = ddg[tid] = 0.0f;
+  {
+    const float* src = chunk_slot(a, g, b, h, c);
+    for (int e = tid * 4; e < g.P * g.N; e += kThreads * 4)
+      *reinterpret_cast<float4*>(S + (e / g.N) * LN + e % g.N) = *reinterpret_cast<const float4*>(src + e);
+  }
+  load_rows(Q, LN, a.q, b, h, R, t0 * R, rows, g.N);
+  load_rows(K, LN, a.k, b, h, R, t0 * R, rows, g.N);
+  load_rows(V, LP, a.v, b, h, R, t0 * R, rows, g.P);
+  load_rows(dY, LP, a.dy, b, h, R, t0 * R, rows, g.P);
+  __syncthreads();
+  // scores A = Q K^T and B = dY V^T (2 x 2 tiles): Wt = L o A, M = L o B, pair terms of dcum / ddiag
+  {
+    const int m0 = (tid / 16) * 2, n0 = (tid % 16) * 2;
+    float qa[2][2], bb[2][2];
+    zero(qa);
+    zero(bb);
+    mm<2, 2, false, false>(qa, Q, LN, K, LN, g.N, m0, n0);
+    mm<2, 2, false, false>(bb, dY, LP, V, LP, g.P, m0, n0);
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = m0 + t, j = n0 + u, ti = i / R, tj = j / R;
+        float w = 0.0f, m = 0.0f;
+        if (i < rows && j < rows && tj <= ti) {
+          if (tj == ti) {
+            const float dg = diag_at(a, b, t0 + ti, h);
+            w = dg * qa[t][u];
+            m = dg * bb[t][u];
+            atomicAdd(&ddg[ti], qa[t][u] * bb[t][u]);
+          } else {
+            const float lw = expf(red[ti] - red[tj]);
+            w = lw * qa[t][u];
+            m = lw * bb[t][u];
+            const float gp = w * bb[t][u];
+            atomicAdd(&dcum[ti], gp);
+            atomicAdd(&dcum[tj], -gp);
+          }
+        }
+        W[i * kLdr + j] = w;
+        M[i * kLdr + j] = m;
+      }
+  }
+  __syncthreads();
+  // dq = e^{cum} (dY S) + M K: 2 x 8 tiles over [kRows][N]
+  {
+    const int tiles_n = g.N / 8;
+    for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
+      const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 8;
+      float inter[2][8], intra[2][8];
+      zero(inter);
+      zero(intra);
+      mm<2, 8, false, true>(inter, dY, LP, S, LN, g.P, m0, n0);
+      mm<2, 8, false, true>(intra, M, kLdr, K, LN, kRows, m0, n0);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int i = m0 + t;
+        if (i >= rows) continue;
+        const int row = t0 * R + i;
+        float* dst = static_cast<float*>(a.dq.data) + row_off(a.dq, b, row / R, h, row % R);
+        const float e = red[kRows + i / R];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) dst[(n0 + u) * a.dq.stride[4]] = fmaf(e, inter[t][u], intra[t][u]);
+      }
+    }
+  }
+  // inter term of dcum: e^{cum_t} dy_i . (S q_i): (Q S^T) in 2 x 4 tiles over [kRows][P]
+  {
+    const int tiles_n = g.P / 4;
+    for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
+      const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 4;
+      float sq[2][4];
+      zero(sq);
+      mm<2, 4, false, false>(sq, Q, LN, S, LN, g.N, m0, n0);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int i = m0 + t;
+        float d = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) d = fmaf(dY[i * LP + n0 + u], sq[t][u], d);
+        if (i < rows) atomicAdd(&dcum[i / R], red[kRows + i / R] * d);
       }
     }
   }
   __syncthreads();
-  if (a.dinitial.data) {
-    const m3_tensor& t = a.dinitial;
-    for (int o = tid; o < P * N; o += kThreads) {
-      const int p = o / N, n = o % N;
-      static_cast<float*>(t.data)[b * t.stride[0] + h * t.stride[1] + p * t.stride[2] + n * t.stride[3]] =
-          s.dS[p * s.ldn + n];
+  // Phase 2: G_c = dLoss/dS_{c+1} replaces S_c
+  {
+    const float* src = grads + (bh * g.nchunk + c) * g.P * g.N;
+    for (int e = tid * 4; e < g.P * g.N; e += kThreads * 4)
+      *reinterpret_cast<float4*>(S + (e / g.N) * LN + e % g.N) = *reinterpret_cast<const float4*>(src + e);
+  }
+  __syncthreads();
+  // dk = T (V G) + M^T Q: 2 x 8 tiles over [kRows][N]
+  {
+    const int tiles_n = g.N / 8;
+    for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
+      const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 8;
+      float st[2][8], pr[2][8];
+      zero(st);
+      zero(pr);
+      mm<2, 8, false, true>(st, V, LP, S, LN, g.P, m0, n0);
+      mm<2, 8, true, true>(pr, M, kLdr, Q, LN, kRows, m0, n0);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int j = m0 + t;
+        if (j >= rows) continue;
+        const int row = t0 * R + j;
+        float* dst = static_cast<float*>(a.dk.data) + row_off(a.dk, b, row / R, h, row % R);
+        const float T = red[2 * kRows + j / R];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) dst[(n0 + u) * a.dk.stride[4]] = fmaf(T, st[t][u], pr[t][u]);
+      }
     }
   }
+  // dv = T (K G^T) + Wt^T dY: 2 x 4 tiles over [kRows][P]; state terms of dcum from v_j . (G k_j)
+  {
+    const int tiles_n = g.P / 4;
+    for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
+      const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 4;
+      float gk[2][4], pr[2][4];
+      zero(gk);
+      zero(pr);
+      mm<2, 4, false, false>(gk, K, LN, S, LN, g.N, m0, n0);
+      mm<2, 4, true, true>(pr, W, kLdr, dY, LP, kRows, m0, n0);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int j = m0 + t;
+        if (j >= rows) continue;
+        const int row = t0 * R + j;
+        float* dst = static_cast<float*>(a.dv.data) + row_off(a.dv, b, row / R, h, row % R);
+        const float T = red[2 * kRows + j / R];
+        float sd = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          dst[(n0 + u) * a.dv.stride[4]] = fmaf(T, gk[t][u], pr[t][u]);
+          sd = fmaf(V[j * LP + n0 + u], gk[t][u], sd);
+        }
+        sd *= T;
+        atomicAdd(&dcum[j / R], -sd);
+        atomicAdd(&dcum[ntok - 1], sd);
+      }
+    }
+  }
+  __syncthreads();
+  // dadt = reverse cumsum of dcum (plus e^{cum_last} <G_c, S_c> on the last token); ddiag
+  if (tid < 32) {
+    const int lane = tid;
+    const float lam = expf(red[ntok - 1]);
+    float v = lane < ntok ? dcum[lane] + (lane == ntok - 1 ? lam * gs[bh * g.nchunk + c] : 0.0f) : 0.0f;
+    for (int off = 1; off < 32; off <<= 1) {
+      const float nb = __shfl_down_sync(0xffffffffu, v, off);
+      if (lane + off < 32) v += nb;
+    }
+    if (lane < ntok) {
+      const m3_tensor& da = a.dadt;
+      static_cast<float*>(da.data)[b * da.stride[0] + (int64_t)(t0 + lane) * da.stride[1] + h * da.stride[2]] = v;
+      const m3_tensor& dd = a.ddiag;
+      static_cast<float*>(dd.data)[b * dd.stride[0] + (int64_t)(t0 + lane) * dd.stride[1] + h * dd.stride[2]] =
+          ddg[lane];
+    }
+  }
+}
+
+inline size_t delta_smem(int N, int P) { return (size_t)(kRows * ldp(P) + kRows * ldn(N) + 3 * kRows) * 4; }
+inline size_t output_smem(int N, int P) {
+  return (size_t)(P * ldn(N) + 2 * kRows * ldn(N) + kRows * ldp(P) + kRows * kLdr + 3 * kRows) * 4;
+}
+inline size_t grads_smem(int N, int P) {
+  return (size_t)(P * ldn(N) + 2 * kRows * ldn(N) + 2 * kRows * ldp(P) + 2 * kRows * kLdr + 5 * kRows) * 4;
 }
 
 }  // namespace ssdt
@@ -365,40 +620,98 @@ int report_error(int code, const char* msg);
 static int ssd_check(const m3_ssd_args* args, bool bwd) {
   if (args == nullptr) return report_error(M3_ERR_ARGUMENT, "null argument struct");
   const m3_ssd_args& a = *args;
-  if (a.batch <= 0 || a.length <= 0 || a.heads <= 0) return report_error(M3_ERR_SHAPE, "batch, length and heads must be positive");
-  if (a.rank != 1 && a.rank != 2 && a.rank != 4 && a.rank != 8) return report_error(M3_ERR_SHAPE, "rank must be 1, 2, 4 or 8");
-  if (a.d_state <= 0 || a.d_state > ssdt::kMaxN || a.head_dim <= 0 || a.head_dim > ssdt::kMaxP)
-    return report_error(M3_ERR_SHAPE, "training kernels serve d_state <= 128 and head_dim <= 64");
+  if (a.batch <= 0 || a.length <= 0 || a.heads <= 0)
+    return report_error(M3_ERR_SHAPE, "batch, length and heads must be positive");
+  if (a.rank != 1 && a.rank != 2 && a.rank != 4 && a.rank != 8)
+    return report_error(M3_ERR_SHAPE, "rank must be 1, 2, 4 or 8");
+  if (a.d_state <= 0 || a.d_state > ssdt::kMaxN || a.head_dim <= 0 || a.head_dim > ssdt::kMaxP ||
+      a.d_state % 8 != 0 || a.head_dim % 8 != 0)
+    return report_error(M3_ERR_SHAPE, "training kernels serve d_state <= 128 and head_dim <= 64, multiples of 8");
   const m3_tensor* need[] = {&a.q, &a.k, &a.v, &a.adt, &a.diag, &a.chunk_states};
   for (const m3_tensor* t : need)
-    if (t->data == nullptr || t->dtype != M3_F32) return report_error(M3_ERR_ARGUMENT, "q, k, v, adt, diag and chunk_states must be float32 tensors");
-  if (a.initial_state.data && a.initial_state.dtype != M3_F32) return report_error(M3_ERR_ARGUMENT, "initial_state must be float32");
+    if (t->data == nullptr || t->dtype != M3_F32)
+      return report_error(M3_ERR_ARGUMENT, "q, k, v, adt, diag and chunk_states must be float32 tensors");
+  if ((reinterpret_cast<uintptr_t>(a.chunk_states.data) & 15u) != 0)
+    return report_error(M3_ERR_LAYOUT, "chunk_states must be 16-byte aligned and contiguous");
+  // row tensors: contiguous rows starting on 16-byte boundaries (16-byte loads)
+  const m3_tensor* row_tensors[] = {&a.q, &a.k, &a.v, &a.dy};
+  for (const m3_tensor* t : row_tensors) {
+    if (t->data == nullptr) continue;
+    if (t->stride[4] != 1 || (reinterpret_cast<uintptr_t>(t->data) & 15u) != 0 || t->stride[0] % 4 != 0 ||
+        t->stride[1] % 4 != 0 || t->stride[2] % 4 != 0 || t->stride[3] % 4 != 0)
+      return report_error(M3_ERR_LAYOUT, "q, k, v and dy need contiguous rows on 16-byte boundaries");
+  }
+  if (a.initial_state.data && a.initial_state.dtype != M3_F32)
+    return report_error(M3_ERR_ARGUMENT, "initial_state must be float32");
   if (!bwd) {
     if (!a.y.data || !a.final_state.data || a.y.dtype != M3_F32 || a.final_state.dtype != M3_F32)
       return report_error(M3_ERR_ARGUMENT, "y and final_state must be float32 outputs");
   } else {
     const m3_tensor* outs[] = {&a.dy, &a.dq, &a.dk, &a.dv, &a.dadt, &a.ddiag};
     for (const m3_tensor* t : outs)
-      if (t->data == nullptr || t->dtype != M3_F32) return report_error(M3_ERR_ARGUMENT, "dy, dq, dk, dv, dadt and ddiag must be float32 tensors");
+      if (t->data == nullptr || t->dtype != M3_F32)
+        return report_error(M3_ERR_ARGUMENT, "dy, dq, dk, dv, dadt and ddiag must be float32 tensors");
     if ((a.dfinal.data && a.dfinal.dtype != M3_F32) || (a.dinitial.data && a.dinitial.dtype != M3_F32))
       return report_error(M3_ERR_ARGUMENT, "dfinal and dinitial must be float32");
   }
+  if (a.workspace.data == nullptr || a.workspace.dtype != M3_F32 ||
+      (reinterpret_cast<uintptr_t>(a.workspace.data) & 15u) != 0)
+    return report_error(M3_ERR_ARGUMENT, "a 16-byte aligned float32 workspace of m3_ssd_workspace_bytes() is required");
   return M3_OK;
 }
 
-static int ssd_launch(const m3_ssd_args* args, void* stream, bool bwd) {
+static int64_t ssd_nchunk(const m3_ssd_args& a) {
+  const int tok_per = ssdt::kRows / a.rank;
+  return (a.length + tok_per - 1) / tok_per;
+}
+
+// Scratch floats of a call: per-chunk e^{cum_last} and <G_c, S_c>, then (backward) the gradient slots.
+static int64_t ssd_scratch_floats(const m3_ssd_args& a, bool bwd) {
+  const int64_t slots = (int64_t)a.batch * a.heads * ssd_nchunk(a);
+  const int64_t small = (2 * slots + 3) / 4 * 4;
+  return small + (bwd ? slots * a.head_dim * a.d_state : 0);
+}
+
+template <typename K> static cudaError_t set_smem(K kern, size_t bytes) {
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+static int ssd_launch(const m3_ssd_args* args, void* stream_, bool bwd) {
   const int rc = ssd_check(args, bwd);
   if (rc != M3_OK) return rc;
   const m3_ssd_args& a = *args;
-  if (a.device >= 0 && cudaSetDevice(a.device) != cudaSuccess) return report_error(M3_ERR_CUDA, "cannot select the device");
-  const size_t smem = ssdt::smem_floats(a.d_state, a.head_dim, bwd) * sizeof(float);
-  auto kern = bwd ? ssdt::ssd_bwd_kernel : ssdt::ssd_fwd_kernel;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e == cudaSuccess) {
-    kern<<<dim3(a.heads, a.batch), ssdt::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
-    e = cudaGetLastError();
+  if (a.device >= 0 && cudaSetDevice(a.device) != cudaSuccess)
+    return report_error(M3_ERR_CUDA, "cannot select the device");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int N = a.d_state, P = a.head_dim;
+  const int64_t nchunk = ssd_nchunk(a);
+  const int64_t slots = (int64_t)a.batch * a.heads * nchunk;
+  float* ws = static_cast<float*>(a.workspace.data);
+  float* lam = ws;
+  float* gs = ws + slots;
+  float* grads = ws + (2 * slots + 3) / 4 * 4;
+  const dim3 chunk_grid((unsigned)nchunk, a.heads, a.batch), bh_grid(a.heads, a.batch);
+  cudaError_t e = set_smem(ssdt::chunk_delta_kernel, ssdt::delta_smem(N, P));
+  if (!bwd) {
+    if (e == cudaSuccess) e = set_smem(ssdt::chunk_output_kernel, ssdt::output_smem(N, P));
+    if (e == cudaSuccess) {
+      ssdt::chunk_delta_kernel<<<chunk_grid, ssdt::kThreads, ssdt::delta_smem(N, P), stream>>>(
+          a, 0, static_cast<float*>(a.chunk_states.data), lam);
+      ssdt::state_scan_kernel<<<bh_grid, ssdt::kThreads, 0, stream>>>(a, lam);
+      ssdt::chunk_output_kernel<<<chunk_grid, ssdt::kThreads, ssdt::output_smem(N, P), stream>>>(a);
+      e = cudaGetLastError();
+    }
+  } else {
+    if (e == cudaSuccess) e = set_smem(ssdt::chunk_grads_kernel, ssdt::grads_smem(N, P));
+    if (e == cudaSuccess) {
+      ssdt::chunk_delta_kernel<<<chunk_grid, ssdt::kThreads, ssdt::delta_smem(N, P), stream>>>(a, 1, grads, lam);
+      ssdt::grad_scan_kernel<<<bh_grid, ssdt::kThreads, 0, stream>>>(a, grads, lam, gs);
+      ssdt::chunk_grads_kernel<<<chunk_grid, ssdt::kThreads, ssdt::grads_smem(N, P), stream>>>(a, grads, gs);
+      e = cudaGetLastError();
+    }
   }
-  if (e != cudaSuccess) return report_error(M3_ERR_CUDA, (std::string("training kernel launch failed: ") + cudaGetErrorString(e)).c_str());
+  if (e != cudaSuccess)
+    return report_error(M3_ERR_CUDA, (std::string("training kernel launch failed: ") + cudaGetErrorString(e)).c_str());
   return M3_OK;
 }
 
@@ -407,6 +720,13 @@ static int ssd_launch(const m3_ssd_args* args, void* stream, bool bwd) {
 extern "C" {
 
 int m3_ssd_chunk_rows(void) { return m3::ssdt::kRows; }
+
+int64_t m3_ssd_workspace_bytes(const m3_ssd_args* args, int backward) {
+  if (args == nullptr) return -m3::report_error(M3_ERR_ARGUMENT, "null argument struct");
+  if (args->batch <= 0 || args->length <= 0 || args->heads <= 0 || args->rank <= 0)
+    return -m3::report_error(M3_ERR_SHAPE, "batch, length, heads and rank must be positive");
+  return m3::ssd_scratch_floats(*args, backward != 0) * (int64_t)sizeof(float);
+}
 
 int m3_ssd_train_fwd(const m3_ssd_args* args, void* stream) { return m3::ssd_launch(args, stream, false); }
 

@@ -77,7 +77,7 @@ def test_training_prelude_and_epilogue_match_the_pytorch_formulation(monkeypatch
 
 def test_training_entry_points_reject_bad_arguments_without_a_device():
     lib = _ext.load()
-    assert ctypes.sizeof(_ext.SSDArgs) == 8 * 4 + 17 * 64
+    assert ctypes.sizeof(_ext.SSDArgs) == 8 * 4 + 18 * 64
     assert lib.m3_ssd_chunk_rows() == 32
     assert lib.m3_ssd_train_fwd(None, None) == 4
     assert lib.m3_ssd_train_bwd(None, None) == 4
