@@ -82,63 +82,47 @@ __device__ inline void chunk_scalars(float* red, const m3_tensor& adt, int b, in
   }
 }
 
-// Register-tiled product: acc[TM][TN] += sum_k A(m0 + t, k) B(k, n0 + u) over k in [0, K) (K a
-// multiple of 4). A is stored k-major (A(m, k) = A[k * lda + m]) when AK, else m-major
-// (A[m * lda + k]); B likewise with BK (B(k, n) = B[k * ldb + n]) or n-major (B[n * ldb + k]).
-// Every shared load is a 16- or 8-byte vector: row starts and strides are multiples of 4 floats.
+// Register-tiled product: acc[t][u] += sum_k A(mi(t), k) B(k, nj(u)) over k in [0, K) (K a multiple
+// of 4). A is stored k-major (A(m, k) = A[k * lda + m]) when AK, else m-major (A[m * lda + k]); B
+// likewise with BK (B(k, n) = B[k * ldb + n]) or n-major (B[n * ldb + k]). Tile indices: a k-major
+// operand is read in 16-byte groups, mi(t) = mb + (t / 4) ms + t % 4; an m-major one row by row,
+// mi(t) = mb + t ms (nj likewise). Threads of a warp take adjacent mb / nb, so their 16-byte shared
+// loads fall on adjacent addresses (k-major) or on rows one padded stride apart (m-/n-major):
+// no bank conflicts.
 template <int TM, int TN, bool AK, bool BK>
 __device__ __forceinline__ void mm(float (&acc)[TM][TN], const float* A, int lda, const float* B, int ldb, int K,
-                                   int m0, int n0) {
-  static_assert(TM % 2 == 0 && TN % 2 == 0, "even tiles");
+                                   int mb, int ms, int nb, int ns) {
+  static_assert(!AK || TM % 4 == 0, "k-major A is read in groups of four");
+  static_assert(!BK || TN % 4 == 0, "k-major B is read in groups of four");
   for (int k = 0; k < K; k += 4) {
     float a[4][TM], bb[4][TN];
     if constexpr (AK) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const float* src = A + (k + kk) * lda + m0;
-        if constexpr (TM % 4 == 0) {
+      for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-          for (int t = 0; t < TM; t += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(src + t);
-            a[kk][t] = v.x, a[kk][t + 1] = v.y, a[kk][t + 2] = v.z, a[kk][t + 3] = v.w;
-          }
-        } else {
-#pragma unroll
-          for (int t = 0; t < TM; t += 2) {
-            const float2 v = *reinterpret_cast<const float2*>(src + t);
-            a[kk][t] = v.x, a[kk][t + 1] = v.y;
-          }
+        for (int t = 0; t < TM; t += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(A + (k + kk) * lda + mb + (t / 4) * ms);
+          a[kk][t] = v.x, a[kk][t + 1] = v.y, a[kk][t + 2] = v.z, a[kk][t + 3] = v.w;
         }
-      }
     } else {
 #pragma unroll
       for (int t = 0; t < TM; ++t) {
-        const float4 v = *reinterpret_cast<const float4*>(A + (m0 + t) * lda + k);
+        const float4 v = *reinterpret_cast<const float4*>(A + (mb + t * ms) * lda + k);
         a[0][t] = v.x, a[1][t] = v.y, a[2][t] = v.z, a[3][t] = v.w;
       }
     }
     if constexpr (BK) {
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const float* src = B + (k + kk) * ldb + n0;
-        if constexpr (TN % 4 == 0) {
+      for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
-          for (int u = 0; u < TN; u += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(src + u);
-            bb[kk][u] = v.x, bb[kk][u + 1] = v.y, bb[kk][u + 2] = v.z, bb[kk][u + 3] = v.w;
-          }
-        } else {
-#pragma unroll
-          for (int u = 0; u < TN; u += 2) {
-            const float2 v = *reinterpret_cast<const float2*>(src + u);
-            bb[kk][u] = v.x, bb[kk][u + 1] = v.y;
-          }
+        for (int u = 0; u < TN; u += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(B + (k + kk) * ldb + nb + (u / 4) * ns);
+          bb[kk][u] = v.x, bb[kk][u + 1] = v.y, bb[kk][u + 2] = v.z, bb[kk][u + 3] = v.w;
         }
-      }
     } else {
 #pragma unroll
       for (int u = 0; u < TN; ++u) {
-        const float4 v = *reinterpret_cast<const float4*>(B + (n0 + u) * ldb + k);
+        const float4 v = *reinterpret_cast<const float4*>(B + (nb + u * ns) * ldb + k);
         bb[0][u] = v.x, bb[1][u] = v.y, bb[2][u] = v.z, bb[3][u] = v.w;
       }
     }
@@ -150,6 +134,10 @@ __device__ __forceinline__ void mm(float (&acc)[TM][TN], const float* A, int lda
         for (int u = 0; u < TN; ++u) acc[t][u] = fmaf(a[kk][t], bb[kk][u], acc[t][u]);
   }
 }
+
+// Tile index of element t: grouped (k-major reads) or row-wise.
+__device__ __forceinline__ int gidx(int base, int stride, int t) { return base + (t >> 2) * stride + (t & 3); }
+__device__ __forceinline__ int ridx(int base, int stride, int t) { return base + t * stride; }
 
 template <int TM, int TN> __device__ __forceinline__ void zero(float (&acc)[TM][TN]) {
 #pragma unroll
@@ -186,6 +174,7 @@ __device__ __forceinline__ float diag_at(const m3_ssd_args& a, int b, int t, int
 
 // delta_c = sum_j w_j x_j y_j^T over the chunk rows ([P][N]) into `out`, with x = v (w = T_s) for the
 // forward or x = dy (w = e^{cum_t}) for the backward, y = k or q. Also writes e^{cum_last} to lam.
+// Thread tile: 4 p x 8 n (two groups of four columns N / 2 apart).
 __global__ void __launch_bounds__(kThreads) chunk_delta_kernel(const m3_ssd_args a, int bwd, float* out, float* lam) {
   extern __shared__ float smem[];
   const Geo g = geo(a);
@@ -200,20 +189,40 @@ __global__ void __launch_bounds__(kThreads) chunk_delta_kernel(const m3_ssd_args
   load_rows(Y, ldn(g.N), bwd ? a.q : a.k, b, h, g.R, t0 * g.R, rows, g.N);
   __syncthreads();
   float* dst = out + (((int64_t)b * a.heads + h) * g.nchunk + c) * g.P * g.N;
-  const int tiles_n = g.N / 8;
-  for (int tile = threadIdx.x; tile < (g.P / 4) * tiles_n; tile += kThreads) {
-    const int m0 = (tile / tiles_n) * 4, n0 = (tile % tiles_n) * 8;
+  const int cn = g.N / 8;  // threads along n
+  for (int tile = threadIdx.x; tile < (g.P / 4) * cn; tile += kThreads) {
+    const int mb = (tile / cn) * 4, nb = (tile % cn) * 4, ns = 4 * cn;
     float acc[4][8];
     zero(acc);
-    mm<4, 8, true, true>(acc, X, ldp(g.P), Y, ldn(g.N), kRows, m0, n0);
+    mm<4, 8, true, true>(acc, X, ldp(g.P), Y, ldn(g.N), kRows, mb, 0, nb, ns);
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      float4* d = reinterpret_cast<float4*>(dst + (m0 + t) * g.N + n0);
-      d[0] = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
-      d[1] = make_float4(acc[t][4], acc[t][5], acc[t][6], acc[t][7]);
-    }
+    for (int t = 0; t < 4; ++t)
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+        *reinterpret_cast<float4*>(dst + (mb + t) * g.N + nb + q * ns) =
+            make_float4(acc[t][4 * q], acc[t][4 * q + 1], acc[t][4 * q + 2], acc[t][4 * q + 3]);
   }
   if (threadIdx.x == 0) lam[((int64_t)b * a.heads + h) * g.nchunk + c] = expf(red[ntok - 1]);
+}
+
+// Loads rows [row0, row0 + rows) of a [B, L, H, R, X] float tensor transposed into dst [X][ld]
+// (dst[x * ld + i]); rows past `rows` are zero.
+__device__ inline void load_rows_t(float* dst, int ld, const m3_tensor& t, int b, int h, int R, int row0, int rows,
+                                   int X) {
+  const float* base = static_cast<const float*>(t.data);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = warp; i < kRows; i += kThreads / 32) {
+    if (4 * lane >= X) continue;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < rows) {
+      const int row = row0 + i;
+      v = *reinterpret_cast<const float4*>(base + row_off(t, b, row / R, h, row % R) + 4 * lane);
+    }
+    dst[(4 * lane) * ld + i] = v.x;
+    dst[(4 * lane + 1) * ld + i] = v.y;
+    dst[(4 * lane + 2) * ld + i] = v.z;
+    dst[(4 * lane + 3) * ld + i] = v.w;
+  }
 }
 
 // Forward carry, per (batch, head): slot c holds delta_c on entry and S_c on exit;
@@ -277,18 +286,18 @@ __global__ void __launch_bounds__(kThreads) state_scan_kernel(const m3_ssd_args 
   }
 }
 
-// y_i = e^{cum_t} S_c q_i + sum_j Wt_ij v_j per chunk.
+// y_i = e^{cum_t} S_c q_i + sum_j Wt_ij v_j per chunk. Row tiles i = im + 16 t; columns p = in + (P/4) u.
 __global__ void __launch_bounds__(kThreads) chunk_output_kernel(const m3_ssd_args a) {
   extern __shared__ float smem[];
   const Geo g = geo(a);
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
   const int t0 = c * g.tok_per, ntok = min(g.tok_per, g.L - t0), rows = ntok * g.R, R = g.R;
-  const int LN = ldn(g.N), LP = ldp(g.P);
+  const int LN = ldn(g.N);
   float* S = smem;                // [P][LN]
   float* Q = S + g.P * LN;        // [kRows][LN]
   float* K = Q + kRows * LN;      // [kRows][LN]
-  float* V = K + kRows * LN;      // [kRows][LP]
-  float* W = V + kRows * LP;      // [kRows][kLdr]
+  float* Vt = K + kRows * LN;     // [P][kLdr]   v transposed
+  float* W = Vt + g.P * kLdr;     // [kRows][kLdr]
   float* red = W + kRows * kLdr;  // [3][kRows]
   chunk_scalars(red, a.adt, b, h, t0, ntok);
   {
@@ -298,19 +307,19 @@ __global__ void __launch_bounds__(kThreads) chunk_output_kernel(const m3_ssd_arg
   }
   load_rows(Q, LN, a.q, b, h, R, t0 * R, rows, g.N);
   load_rows(K, LN, a.k, b, h, R, t0 * R, rows, g.N);
-  load_rows(V, LP, a.v, b, h, R, t0 * R, rows, g.P);
+  load_rows_t(Vt, kLdr, a.v, b, h, R, t0 * R, rows, g.P);
   __syncthreads();
-  // Wt = L o (Q K^T): 2 x 2 tiles
+  // W = L o (Q K^T): 2 x 2 tiles, i = im + 16 t, j = in + 16 u
   {
-    const int m0 = (tid / 16) * 2, n0 = (tid % 16) * 2;
+    const int im = tid / 16, in = tid % 16;
     float acc[2][2];
     zero(acc);
-    mm<2, 2, false, false>(acc, Q, LN, K, LN, g.N, m0, n0);
+    mm<2, 2, false, false>(acc, Q, LN, K, LN, g.N, im, 16, in, 16);
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
-        const int i = m0 + t, j = n0 + u, ti = i / R, tj = j / R;
+        const int i = im + 16 * t, j = in + 16 * u, ti = i / R, tj = j / R;
         float w = 0.0f;
         if (i < rows && j < rows && tj <= ti)
           w = (tj < ti ? expf(red[ti] - red[tj]) : diag_at(a, b, t0 + ti, h)) * acc[t][u];
@@ -319,23 +328,23 @@ __global__ void __launch_bounds__(kThreads) chunk_output_kernel(const m3_ssd_arg
   }
   __syncthreads();
   // y = e^{cum} (Q S^T) + W V: 2 x 4 tiles over [kRows][P]
-  const int tiles_n = g.P / 4;
-  for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
-    const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 4;
+  const int cn = g.P / 4;
+  for (int tile = tid; tile < 16 * cn; tile += kThreads) {
+    const int im = tile / cn, in = tile % cn;
     float inter[2][4], intra[2][4];
     zero(inter);
     zero(intra);
-    mm<2, 4, false, false>(inter, Q, LN, S, LN, g.N, m0, n0);
-    mm<2, 4, false, true>(intra, W, kLdr, V, LP, kRows, m0, n0);
+    mm<2, 4, false, false>(inter, Q, LN, S, LN, g.N, im, 16, in, cn);
+    mm<2, 4, false, false>(intra, W, kLdr, Vt, kLdr, kRows, im, 16, in, cn);
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      const int i = m0 + t;
+      const int i = im + 16 * t;
       if (i >= rows) continue;
       const int row = t0 * R + i;
       float* dst = static_cast<float*>(a.y.data) + row_off(a.y, b, row / R, h, row % R);
       const float e = red[kRows + i / R];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) dst[(n0 + u) * a.y.stride[4]] = fmaf(e, inter[t][u], intra[t][u]);
+      for (int u = 0; u < 4; ++u) dst[(in + cn * u) * a.y.stride[4]] = fmaf(e, inter[t][u], intra[t][u]);
     }
   }
 }
@@ -420,8 +429,10 @@ __global__ void __launch_bounds__(kThreads) grad_scan_kernel(const m3_ssd_args a
   }
 }
 
-// Per-chunk gradients. Phase 1 (S_c in shared memory): scores, Wt, M, the pair terms of dcum/ddiag,
-// dq and the inter term of dcum. Phase 2 (G_c replaces S_c): dk, dv and the state terms of dcum.
+// Per-chunk gradients. Phase 1 (S_c in shared memory): scores, M, M^T, W^T, the pair terms of
+// dcum / ddiag, dq and the inter term of dcum. Phase 2 (G_c replaces S_c): dk, dv and the state
+// terms of dcum. Row tiles i (or j) = im + 16 t; columns n = 4 in + 64 (u / 4) + u % 4 (grouped) or
+// p = in + (P/4) u (row-wise).
 __global__ void __launch_bounds__(kThreads) chunk_grads_kernel(const m3_ssd_args a, const float* grads,
                                                                const float* gs) {
   extern __shared__ float smem[];
@@ -429,14 +440,16 @@ __global__ void __launch_bounds__(kThreads) chunk_grads_kernel(const m3_ssd_args
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
   const int t0 = c * g.tok_per, ntok = min(g.tok_per, g.L - t0), rows = ntok * g.R, R = g.R;
   const int LN = ldn(g.N), LP = ldp(g.P);
-  float* S = smem;                // [P][LN]: S_c, then G_c
-  float* Q = S + g.P * LN;        // [kRows][LN]
-  float* K = Q + kRows * LN;      // [kRows][LN]
-  float* V = K + kRows * LN;      // [kRows][LP]
-  float* dY = V + kRows * LP;     // [kRows][LP]
-  float* W = dY + kRows * LP;     // [kRows][kLdr]
-  float* M = W + kRows * kLdr;    // [kRows][kLdr]
-  float* red = M + kRows * kLdr;  // cum, e^cum, T, dcum, ddiag  [5][kRows]
+  float* S = smem;                 // [P][LN]: S_c, then G_c
+  float* Q = S + g.P * LN;         // [kRows][LN]
+  float* K = Q + kRows * LN;       // [kRows][LN]
+  float* V = K + kRows * LN;       // [kRows][LP]
+  float* dY = V + kRows * LP;      // [kRows][LP]
+  float* dYt = dY + kRows * LP;    // [P][kLdr]
+  float* M = dYt + g.P * kLdr;     // [kRows][kLdr]  L o (dY V^T)
+  float* Mt = M + kRows * kLdr;    // [kRows][kLdr]  its transpose
+  float* Wt = Mt + kRows * kLdr;   // [kRows][kLdr]  (L o (Q K^T))^T
+  float* red = Wt + kRows * kLdr;  // cum, e^cum, T, dcum, ddiag  [5][kRows]
   float* dcum = red + 3 * kRows;
   float* ddg = red + 4 * kRows;
   const int64_t bh = (int64_t)b * a.heads + h;
@@ -451,20 +464,21 @@ __global__ void __launch_bounds__(kThreads) chunk_grads_kernel(const m3_ssd_args
   load_rows(K, LN, a.k, b, h, R, t0 * R, rows, g.N);
   load_rows(V, LP, a.v, b, h, R, t0 * R, rows, g.P);
   load_rows(dY, LP, a.dy, b, h, R, t0 * R, rows, g.P);
+  load_rows_t(dYt, kLdr, a.dy, b, h, R, t0 * R, rows, g.P);
   __syncthreads();
-  // scores A = Q K^T and B = dY V^T (2 x 2 tiles): Wt = L o A, M = L o B, pair terms of dcum / ddiag
+  // scores A = Q K^T and B = dY V^T (2 x 2 tiles): Wt, M, Mt, pair terms of dcum / ddiag
   {
-    const int m0 = (tid / 16) * 2, n0 = (tid % 16) * 2;
+    const int im = tid / 16, in = tid % 16;
     float qa[2][2], bb[2][2];
     zero(qa);
     zero(bb);
-    mm<2, 2, false, false>(qa, Q, LN, K, LN, g.N, m0, n0);
-    mm<2, 2, false, false>(bb, dY, LP, V, LP, g.P, m0, n0);
+    mm<2, 2, false, false>(qa, Q, LN, K, LN, g.N, im, 16, in, 16);
+    mm<2, 2, false, false>(bb, dY, LP, V, LP, g.P, im, 16, in, 16);
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
-        const int i = m0 + t, j = n0 + u, ti = i / R, tj = j / R;
+        const int i = im + 16 * t, j = in + 16 * u, ti = i / R, tj = j / R;
         float w = 0.0f, m = 0.0f;
         if (i < rows && j < rows && tj <= ti) {
           if (tj == ti) {
@@ -481,49 +495,45 @@ __global__ void __launch_bounds__(kThreads) chunk_grads_kernel(const m3_ssd_args
             atomicAdd(&dcum[tj], -gp);
           }
         }
-        W[i * kLdr + j] = w;
+        Wt[j * kLdr + i] = w;
         M[i * kLdr + j] = m;
+        Mt[j * kLdr + i] = m;
       }
   }
   __syncthreads();
+  const int cn8 = g.N / 8, cn4 = g.P / 4;
   // dq = e^{cum} (dY S) + M K: 2 x 8 tiles over [kRows][N]
-  {
-    const int tiles_n = g.N / 8;
-    for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
-      const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 8;
-      float inter[2][8], intra[2][8];
-      zero(inter);
-      zero(intra);
-      mm<2, 8, false, true>(inter, dY, LP, S, LN, g.P, m0, n0);
-      mm<2, 8, false, true>(intra, M, kLdr, K, LN, kRows, m0, n0);
+  for (int tile = tid; tile < 16 * cn8; tile += kThreads) {
+    const int im = tile / cn8, nb = (tile % cn8) * 4, ns = 4 * cn8;
+    float inter[2][8], intra[2][8];
+    zero(inter);
+    zero(intra);
+    mm<2, 8, false, true>(inter, dY, LP, S, LN, g.P, im, 16, nb, ns);
+    mm<2, 8, false, true>(intra, M, kLdr, K, LN, kRows, im, 16, nb, ns);
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int i = m0 + t;
-        if (i >= rows) continue;
-        const int row = t0 * R + i;
-        float* dst = static_cast<float*>(a.dq.data) + row_off(a.dq, b, row / R, h, row % R);
-        const float e = red[kRows + i / R];
+    for (int t = 0; t < 2; ++t) {
+      const int i = im + 16 * t;
+      if (i >= rows) continue;
+      const int row = t0 * R + i;
+      float* dst = static_cast<float*>(a.dq.data) + row_off(a.dq, b, row / R, h, row % R);
+      const float e = red[kRows + i / R];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) dst[(n0 + u) * a.dq.stride[4]] = fmaf(e, inter[t][u], intra[t][u]);
-      }
+      for (int u = 0; u < 8; ++u) dst[gidx(nb, ns, u) * a.dq.stride[4]] = fmaf(e, inter[t][u], intra[t][u]);
     }
   }
   // inter term of dcum: e^{cum_t} dy_i . (S q_i): (Q S^T) in 2 x 4 tiles over [kRows][P]
-  {
-    const int tiles_n = g.P / 4;
-    for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
-      const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 4;
-      float sq[2][4];
-      zero(sq);
-      mm<2, 4, false, false>(sq, Q, LN, S, LN, g.N, m0, n0);
+  for (int tile = tid; tile < 16 * cn4; tile += kThreads) {
+    const int im = tile / cn4, in = tile % cn4;
+    float sq[2][4];
+    zero(sq);
+    mm<2, 4, false, false>(sq, Q, LN, S, LN, g.N, im, 16, in, cn4);
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int i = m0 + t;
-        float d = 0.0f;
+    for (int t = 0; t < 2; ++t) {
+      const int i = im + 16 * t;
+      float d = 0.0f;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) d = fmaf(dY[i * LP + n0 + u], sq[t][u], d);
-        if (i < rows) atomicAdd(&dcum[i / R], red[kRows + i / R] * d);
-      }
+      for (int u = 0; u < 4; ++u) d = fmaf(dY[i * LP + in + cn4 * u], sq[t][u], d);
+      if (i < rows) atomicAdd(&dcum[i / R], red[kRows + i / R] * d);
     }
   }
   __syncthreads();
@@ -535,54 +545,50 @@ __global__ void __launch_bounds__(kThreads) chunk_grads_kernel(const m3_ssd_args
   }
   __syncthreads();
   // dk = T (V G) + M^T Q: 2 x 8 tiles over [kRows][N]
-  {
-    const int tiles_n = g.N / 8;
-    for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
-      const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 8;
-      float st[2][8], pr[2][8];
-      zero(st);
-      zero(pr);
-      mm<2, 8, false, true>(st, V, LP, S, LN, g.P, m0, n0);
-      mm<2, 8, true, true>(pr, M, kLdr, Q, LN, kRows, m0, n0);
+  for (int tile = tid; tile < 16 * cn8; tile += kThreads) {
+    const int im = tile / cn8, nb = (tile % cn8) * 4, ns = 4 * cn8;
+    float st[2][8], pr[2][8];
+    zero(st);
+    zero(pr);
+    mm<2, 8, false, true>(st, V, LP, S, LN, g.P, im, 16, nb, ns);
+    mm<2, 8, false, true>(pr, Mt, kLdr, Q, LN, kRows, im, 16, nb, ns);
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int j = m0 + t;
-        if (j >= rows) continue;
-        const int row = t0 * R + j;
-        float* dst = static_cast<float*>(a.dk.data) + row_off(a.dk, b, row / R, h, row % R);
-        const float T = red[2 * kRows + j / R];
+    for (int t = 0; t < 2; ++t) {
+      const int j = im + 16 * t;
+      if (j >= rows) continue;
+      const int row = t0 * R + j;
+      float* dst = static_cast<float*>(a.dk.data) + row_off(a.dk, b, row / R, h, row % R);
+      const float T = red[2 * kRows + j / R];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) dst[(n0 + u) * a.dk.stride[4]] = fmaf(T, st[t][u], pr[t][u]);
-      }
+      for (int u = 0; u < 8; ++u) dst[gidx(nb, ns, u) * a.dk.stride[4]] = fmaf(T, st[t][u], pr[t][u]);
     }
   }
-  // dv = T (K G^T) + Wt^T dY: 2 x 4 tiles over [kRows][P]; state terms of dcum from v_j . (G k_j)
-  {
-    const int tiles_n = g.P / 4;
-    for (int tile = tid; tile < (kRows / 2) * tiles_n; tile += kThreads) {
-      const int m0 = (tile / tiles_n) * 2, n0 = (tile % tiles_n) * 4;
-      float gk[2][4], pr[2][4];
-      zero(gk);
-      zero(pr);
-      mm<2, 4, false, false>(gk, K, LN, S, LN, g.N, m0, n0);
-      mm<2, 4, true, true>(pr, W, kLdr, dY, LP, kRows, m0, n0);
+  // dv = T (K G^T) + Wt dY^T... per element: T (G k_j)[p] + sum_i Wt_ji dy_i[p]; 2 x 4 tiles over
+  // [kRows][P]; state terms of dcum from v_j . (G k_j)
+  for (int tile = tid; tile < 16 * cn4; tile += kThreads) {
+    const int im = tile / cn4, in = tile % cn4;
+    float gk[2][4], pr[2][4];
+    zero(gk);
+    zero(pr);
+    mm<2, 4, false, false>(gk, K, LN, S, LN, g.N, im, 16, in, cn4);
+    mm<2, 4, false, false>(pr, Wt, kLdr, dYt, kLdr, kRows, im, 16, in, cn4);
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int j = m0 + t;
-        if (j >= rows) continue;
-        const int row = t0 * R + j;
-        float* dst = static_cast<float*>(a.dv.data) + row_off(a.dv, b, row / R, h, row % R);
-        const float T = red[2 * kRows + j / R];
-        float sd = 0.0f;
+    for (int t = 0; t < 2; ++t) {
+      const int j = im + 16 * t;
+      if (j >= rows) continue;
+      const int row = t0 * R + j;
+      float* dst = static_cast<float*>(a.dv.data) + row_off(a.dv, b, row / R, h, row % R);
+      const float T = red[2 * kRows + j / R];
+      float sd = 0.0f;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          dst[(n0 + u) * a.dv.stride[4]] = fmaf(T, gk[t][u], pr[t][u]);
-          sd = fmaf(V[j * LP + n0 + u], gk[t][u], sd);
-        }
-        sd *= T;
-        atomicAdd(&dcum[j / R], -sd);
-        atomicAdd(&dcum[ntok - 1], sd);
+      for (int u = 0; u < 4; ++u) {
+        const int pp = in + cn4 * u;
+        dst[pp * a.dv.stride[4]] = fmaf(T, gk[t][u], pr[t][u]);
+        sd = fmaf(V[j * LP + pp], gk[t][u], sd);
       }
+      sd *= T;
+      atomicAdd(&dcum[j / R], -sd);
+      atomicAdd(&dcum[ntok - 1], sd);
     }
   }
   __syncthreads();
@@ -607,10 +613,11 @@ __global__ void __launch_bounds__(kThreads) chunk_grads_kernel(const m3_ssd_args
 
 inline size_t delta_smem(int N, int P) { return (size_t)(kRows * ldp(P) + kRows * ldn(N) + 3 * kRows) * 4; }
 inline size_t output_smem(int N, int P) {
-  return (size_t)(P * ldn(N) + 2 * kRows * ldn(N) + kRows * ldp(P) + kRows * kLdr + 3 * kRows) * 4;
+  return (size_t)(P * ldn(N) + 2 * kRows * ldn(N) + P * kLdr + kRows * kLdr + 3 * kRows) * 4;
 }
 inline size_t grads_smem(int N, int P) {
-  return (size_t)(P * ldn(N) + 2 * kRows * ldn(N) + 2 * kRows * ldp(P) + 2 * kRows * kLdr + 5 * kRows) * 4;
+  return (size_t)(P * ldn(N) + 2 * kRows * ldn(N) + 2 * kRows * ldp(P) + P * kLdr + 3 * kRows * kLdr + 5 * kRows) *
+         4;
 }
 
 }  // namespace ssdt
