@@ -846,6 +846,172 @@ __global__ void __launch_bounds__(kStepThreads) step_stream_kernel(const m3_step
   }
 }
 
+// mma.sync m16n8k16 (A row-major, B column-major, 16-bit inputs, FP32 accumulate): d += a b.
+template <typename T> __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                               uint32_t b1);
+template <> __device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4],
+                                                                    uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <> __device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                             uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <typename T> __device__ __forceinline__ uint32_t pack_t2(float lo, float hi) {
+  T e[2] = {from_f<T>(lo), from_f<T>(hi)};
+  return *reinterpret_cast<const uint32_t*>(e);
+}
+
+// Stream pass for ranks 2, 4 and 8 (N = 128, P = 64, 16-bit activations) with the rank-structured
+// products on the tensor cores. One CTA per (batch, head); warp w owns state rows 16 w .. 16 w + 15,
+// held in the m16n8 accumulator layout (lane = 4 g + t: rows g and g + 8, columns 2t, 2t + 1 of
+// every 8-column tile). Per 16-column block:
+//   U1 = XP KP, U2 = X K       (one m16n8k16 MMA each per 8-column tile; A = the rank values
+//                               xp_r[p], x_r[p] with the ranks padded to 16, B = the previous /
+//                               current k_r[n] from shared memory)
+//   S' = alpha S + beta U1 + gamma U2     (FP32 on the CUDA cores; streamed store)
+//   Y += bf16(S') Q            (the two S' tiles are the A operand of one MMA, B = q_r[n])
+// The rank values and k are 16-bit values (rounded where the reference rounds them), so every
+// product is exact and only the FP32 summation order differs from step_stream_kernel. All of the
+// warp's state loads are issued before it waits for the prep pass.
+template <typename T, int R>
+__global__ void __launch_bounds__(kStepThreads) step_stream_mma_kernel(const m3_step_args a) {
+  constexpr int N = 128, KR = 8, LQ = N + 8;
+  static_assert(R >= 2 && R <= KR, "ranks 2 .. 8");
+  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const int pr0 = 16 * warp + g, pr1 = pr0 + 8;  // this lane's two state rows
+  __shared__ __align__(16) uint16_t kT[N][KR], kpT[N][KR];  // k_r[n], previous k_r[n], transposed
+  __shared__ __align__(16) uint16_t qs[KR][LQ];              // q_r[n]
+  const float* st = static_cast<const float*>(a.state.data) + b * a.state.stride[0] + h * a.state.stride[1];
+  float* so = static_cast<float*>(a.out_state.data) + b * a.out_state.stride[0] + h * a.out_state.stride[1];
+  const int64_t ss = a.state.stride[2], os = a.out_state.stride[2];
+  // state fragments of all 8 column blocks: [block][tile c * 2 + row half]
+  float2 sv[8][4];
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int n = 16 * nb + 8 * c + 2 * t;
+      sv[nb][2 * c] = __ldcs(reinterpret_cast<const float2*>(st + pr0 * ss + n));
+      sv[nb][2 * c + 1] = __ldcs(reinterpret_cast<const float2*>(st + pr1 * ss + n));
+    }
+  // per-row inputs of rows pr0 / pr1 (independent of the prep pass)
+  const int64_t vb = b * a.value.stride[0] + h * a.value.stride[1];
+  const int64_t pb = b * a.prev_value.stride[0] + h * a.prev_value.stride[1];
+  const int64_t zb = b * a.gate.stride[0] + h * a.gate.stride[1];
+  float x[2], xp[2], z[2], mx[2][2], mz[2][2], mo[2][2];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int p = hr ? pr1 : pr0;
+    x[hr] = ld_t(a.value, vb + p * a.value.stride[2]);
+    xp[hr] = ld_t(a.prev_value, pb + p * a.prev_value.stride[2]);
+    z[hr] = ld_t(a.gate, zb + p * a.gate.stride[2]);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int r = 2 * t + e;
+      mx[hr][e] = mz[hr][e] = mo[hr][e] = 0.0f;
+      if (r < R) {
+        mx[hr][e] = rnd<T>(ld_t(a.mimo_x, h * a.mimo_x.stride[0] + r * a.mimo_x.stride[1] + p * a.mimo_x.stride[2]));
+        mz[hr][e] = rnd<T>(ld_t(a.mimo_z, h * a.mimo_z.stride[0] + r * a.mimo_z.stride[1] + p * a.mimo_z.stride[2]));
+        mo[hr][e] = ld_t(a.mimo_out, h * a.mimo_out.stride[0] + r * a.mimo_out.stride[1] + p * a.mimo_out.stride[2]);
+      }
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // q, k (workspace, activation type) and the previous k into shared memory; ranks >= R are zero
+  const float* ws = static_cast<const float*>(a.workspace.data) + ((int64_t)b * a.heads + h) * (2 * R * N + 4);
+  const uint16_t* wsq = reinterpret_cast<const uint16_t*>(ws);
+  const m3_tensor& pk = a.prev_k;
+  const int64_t kb = b * pk.stride[0] + h * pk.stride[1];
+  for (int i = tid; i < KR * N; i += kStepThreads) {
+    const int r = i / N, n = i % N;
+    uint16_t qv = 0, kv = 0, kpv = 0;
+    if (r < R) {
+      qv = wsq[r * N + n];
+      kv = wsq[R * N + r * N + n];
+      const T e = from_f<T>(ld_t(pk, kb + r * pk.stride[2] + n * pk.stride[3]));
+      kpv = *reinterpret_cast<const uint16_t*>(&e);
+    }
+    qs[r][n] = qv;
+    kT[n][r] = kv;
+    kpT[n][r] = kpv;
+  }
+  const float4 sc = *reinterpret_cast<const float4*>(ws + 2 * R * N);  // alpha, beta, gamma, D
+  // A fragments of the rank values: rows g / g + 8, rank columns 2t, 2t + 1 (upper 8 columns zero)
+  float xr[2][2], zr[2][2];
+  uint32_t ax[4] = {0u, 0u, 0u, 0u}, axp[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    float xv[2], xpv[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      xv[e] = rnd<T>(x[hr] * mx[hr][e]);
+      xpv[e] = rnd<T>(xp[hr] * mx[hr][e]);
+      xr[hr][e] = xv[e];
+      zr[hr][e] = rnd<T>(z[hr] * mz[hr][e]);
+    }
+    ax[hr] = pack_t2<T>(xv[0], xv[1]);
+    axp[hr] = pack_t2<T>(xpv[0], xpv[1]);
+  }
+  __syncthreads();
+  float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb) {
+    float ns[2][4];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int nc = 16 * nb + 8 * c + g;  // B column of this lane (ranks 2t, 2t + 1)
+      const uint32_t bk = *reinterpret_cast<const uint32_t*>(&kT[nc][2 * t]);
+      const uint32_t bkp = *reinterpret_cast<const uint32_t*>(&kpT[nc][2 * t]);
+      float u1[4] = {0.f, 0.f, 0.f, 0.f}, u2[4] = {0.f, 0.f, 0.f, 0.f};
+      mma16816<T>(u1, axp, bkp, 0u);
+      mma16816<T>(u2, ax, bk, 0u);
+      const float2 s0 = sv[nb][2 * c], s1 = sv[nb][2 * c + 1];
+      ns[c][0] = sc.x * s0.x + sc.y * u1[0] + sc.z * u2[0];
+      ns[c][1] = sc.x * s0.y + sc.y * u1[1] + sc.z * u2[1];
+      ns[c][2] = sc.x * s1.x + sc.y * u1[2] + sc.z * u2[2];
+      ns[c][3] = sc.x * s1.y + sc.y * u1[3] + sc.z * u2[3];
+      const int n = 16 * nb + 8 * c + 2 * t;
+      __stcs(reinterpret_cast<float2*>(so + pr0 * os + n), make_float2(ns[c][0], ns[c][1]));
+      __stcs(reinterpret_cast<float2*>(so + pr1 * os + n), make_float2(ns[c][2], ns[c][3]));
+    }
+    // Y += bf16(S') Q over these 16 columns: A = the two S' tiles, B = q_g[n] (rank g)
+    const uint32_t a2[4] = {pack_t2<T>(ns[0][0], ns[0][1]), pack_t2<T>(ns[0][2], ns[0][3]),
+                            pack_t2<T>(ns[1][0], ns[1][1]), pack_t2<T>(ns[1][2], ns[1][3])};
+    const uint32_t bq0 = *reinterpret_cast<const uint32_t*>(&qs[g][16 * nb + 2 * t]);
+    const uint32_t bq1 = *reinterpret_cast<const uint32_t*>(&qs[g][16 * nb + 8 + 2 * t]);
+    mma16816<T>(y, a2, bq0, bq1);
+  }
+  // y fragment: (row g, ranks 2t, 2t + 1), (row g + 8, ranks 2t, 2t + 1);
+  // out_p = sum_r mo_r silu(z mz_r) (S' q_r + D x mx_r), ranks summed across the four lanes t
+  float o[2];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float zz = zr[hr][e];
+      acc += (y[2 * hr + e] + sc.w * xr[hr][e]) * __fdividef(zz, 1.0f + __expf(-zz)) * mo[hr][e];
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    o[hr] = acc;
+  }
+  if (t == 0) {
+    T* yp = static_cast<T*>(a.y.data) + b * a.y.stride[0] + h * a.y.stride[1];
+    yp[pr0 * a.y.stride[2]] = from_f<T>(o[0]);
+    yp[pr1 * a.y.stride[2]] = from_f<T>(o[1]);
+  }
+}
+
 // Name of the step kernel variant the last launch_step on this host thread chose.
 thread_local const char* g_last_step_kernel = "none";
 
@@ -873,6 +1039,21 @@ static cudaError_t launch_step_two_pass(const m3_step_args& a, cudaStream_t stre
                          pk.stride[0] % 4 == 0 && pk.stride[1] % 4 == 0 && pk.stride[2] % 4 == 0;
   // Programmatic dependent launch: the stream pass starts while the prep pass runs and waits for it
   // (griddepcontrol.wait) only after issuing its state loads.
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  if constexpr (R > 1 && sizeof(T) == 2) {
+    if (a.d_state == 128 && a.head_dim == 64) {
+      g_last_step_kernel = "two_pass_mma";
+      cudaLaunchConfig_t mc = {};
+      mc.gridDim = dim3(a.heads, a.batch);
+      mc.blockDim = dim3(kStepThreads);
+      mc.stream = stream;
+      mc.attrs = pdl;
+      mc.numAttrs = 1;
+      return cudaLaunchKernelEx(&mc, step_stream_mma_kernel<T, R>, a);
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.head_dim + rows - 1) / rows, a.heads, a.batch);
   cfg.blockDim = dim3(kStepThreads);

@@ -224,7 +224,7 @@ def test_two_pass_decode_kernels_against_oracle(rank, dtype):
             ex(C), ex(B), cu(v), cu(z), cu(decay), cu(delta), cu(tr), cu(ang), cu(D), tuple(map(cu, cache)),
             q_bias=cu(qb), k_bias=cu(kb), q_norm_w=cu(wq), k_norm_w=cu(wk), dt_bias=cu(bias), norm_eps=1e-5,
             **{key: cu(val) for key, val in mimo.items()})
-    assert _ext.last_step_kernel() == ("two_pass_vec" if rank > 1 else "two_pass")
+    assert _ext.last_step_kernel() == ("two_pass_mma" if rank > 1 else "two_pass")
     d = lambda x: None if x is None else x.double().numpy()
     qn = O.rms_norm(d(C)[:, 0], d(wq))  # [B, R, N]
     kn = O.rms_norm(d(B)[:, 0], d(wk))
@@ -258,7 +258,7 @@ def test_bf16_graph_decoder_at_batch_64_against_oracle(rank):
             dst.copy_(src)
         outs = [decoder(x[:, t:t + 1]).clone() for t in range(prefix, prefix + steps)]
     torch.cuda.synchronize()
-    assert _ext.last_step_kernel() == ("two_pass_vec" if rank > 1 else "two_pass")
+    assert _ext.last_step_kernel() == ("two_pass_mma" if rank > 1 else "two_pass")
     xn = _np(x)
     _, caches = O.model_prefill(cfg, sd, xn[:, :prefix])
     expected = []

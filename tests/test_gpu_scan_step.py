@@ -235,7 +235,7 @@ def test_step_model_mode_matches_preprocessed_inputs(rank, dtype, two_pass):
         y1, c1 = ops._step_device(ex(C), ex(B), v, z, decay, delta, tr, ang, D, cache, q_bias=qb, k_bias=kb,
                                   q_norm_w=wq, k_norm_w=wk, dt_bias=bias, norm_eps=eps, **mimo)
     if two_pass:
-        assert _ext.last_step_kernel() == ("two_pass_vec" if rank > 1 and dtype != torch.float32 else "two_pass")
+        assert _ext.last_step_kernel() == ("two_pass_mma" if rank > 1 and dtype != torch.float32 else "two_pass")
     else:
         assert _ext.last_step_kernel() == "single"
     tol = 1e-5 if dtype == torch.float32 else 1e-2
