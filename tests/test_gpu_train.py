@@ -28,7 +28,7 @@ def _grads(fn, args, kw, targets, seed=11):
     return y.detach(), s.detach(), torch.autograd.grad(loss, targets)
 
 
-@pytest.mark.parametrize("rank", [1, 2, 4])
+@pytest.mark.parametrize("rank", [1, 2, 4, 8])
 @pytest.mark.parametrize("cache", [True, False])
 @pytest.mark.parametrize("length", [45, 200])
 def test_training_kernels_match_autograd_fp32(rank, cache, length):
