@@ -462,7 +462,7 @@ def run_train(world, steps=5):
                                 "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s",
                                 "frac": flops / (kern_ms / 1e3) / 1e12 / FP32_NOMINAL_TFLOPS,
                                 "peak_kind": "nominal", "flops_per_launch_pair": flops},
-           "gpu_launches": 6 * (steps + 2)}
+           "gpu_launches": 8 * (steps + 2)}
     if world == 1:
         try:
             import_reference()

@@ -216,6 +216,30 @@ typedef struct m3_ssd_args {
   m3_tensor workspace; /* float32, 16-byte aligned, m3_ssd_workspace_bytes(args, backward) bytes */
 } m3_ssd_args;
 
+/*
+ * Training prelude of the SSD core, fused: per (batch, token, head, rank) row, qb = q_g + q_bias,
+ * kb = k_g + k_bias (g = the head's Q/K group), rotated by `phase` (SISO pairs (2m, 2m + 1), MIMO
+ * pairs (m, 2S + m); mamba3/ops.py:35-84), k additionally times scale (the trapezoid scale,
+ * ops.py:665-676), each step rounded to the activation dtype as the reference's tensor ops round;
+ * written as float32 rows qf, kc [B,L,H,R,N]. The backward writes the gradients of the biased,
+ * unrotated rows (dqb, dkb [B,L,H,R,N]), of the phase (dphase [B,L,H,S], may be null) and of the
+ * scale (dscale [B,L,H]); the caller sums dqb over the heads of a group and over tokens for the
+ * q / bias gradients. q, k [B,L,G,R,N] in the activation dtype; biases [H,R,N] or null; phase
+ * [B,L,H,S] float32 or null; scale [B,L,H] float32. d_state <= 128, a multiple of 4 (MIMO angle
+ * count a multiple of 4); float32 rows contiguous and 16-byte aligned.
+ */
+typedef struct m3_prelude_args {
+  int32_t batch, length, groups, heads, rank, d_state, num_angles, mimo_rotation;
+  int32_t device; /* CUDA device ordinal of every tensor and of `stream` (-1: current) */
+  int32_t reserved;
+  m3_tensor q, k, q_bias, k_bias, phase, scale;
+  m3_tensor qf, kc;
+  m3_tensor dqf, dkc, dqb, dkb, dphase, dscale;
+} m3_prelude_args;
+
+int m3_ssd_prelude_fwd(const m3_prelude_args* args, void* stream);
+int m3_ssd_prelude_bwd(const m3_prelude_args* args, void* stream);
+
 /* Rows (token, rank) per chunk of the training kernels. */
 int m3_ssd_chunk_rows(void);
 

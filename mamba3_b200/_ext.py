@@ -81,6 +81,16 @@ _SSD_TENSORS = (
 )
 
 
+_PRELUDE_TENSORS = ("q", "k", "q_bias", "k_bias", "phase", "scale", "qf", "kc",
+                    "dqf", "dkc", "dqb", "dkb", "dphase", "dscale")
+
+
+class PreludeArgs(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int32) for name in (
+        "batch", "length", "groups", "heads", "rank", "d_state", "num_angles", "mimo_rotation", "device",
+        "reserved")] + [(name, M3Tensor) for name in _PRELUDE_TENSORS]
+
+
 class SSDArgs(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in (
         "batch", "length", "heads", "rank", "d_state", "head_dim", "device", "reserved")] + [
@@ -135,6 +145,10 @@ def load() -> ctypes.CDLL:
         lib.m3_last_step_kernel.restype = ctypes.c_char_p
         lib.m3_ssd_chunk_rows.argtypes = []
         lib.m3_ssd_chunk_rows.restype = ctypes.c_int
+        lib.m3_ssd_prelude_fwd.argtypes = [ctypes.POINTER(PreludeArgs), ctypes.c_void_p]
+        lib.m3_ssd_prelude_fwd.restype = ctypes.c_int
+        lib.m3_ssd_prelude_bwd.argtypes = [ctypes.POINTER(PreludeArgs), ctypes.c_void_p]
+        lib.m3_ssd_prelude_bwd.restype = ctypes.c_int
         lib.m3_ssd_workspace_bytes.argtypes = [ctypes.POINTER(SSDArgs), ctypes.c_int]
         lib.m3_ssd_workspace_bytes.restype = ctypes.c_int64
         lib.m3_ssd_train_fwd.argtypes = [ctypes.POINTER(SSDArgs), ctypes.c_void_p]
@@ -396,3 +410,46 @@ def ssd_train_backward(q, k, v, adt, diag, chunk_states, dy, dfinal, want_initia
     stream = torch.cuda.current_stream(dev).cuda_stream
     _check(lib.m3_ssd_train_bwd(ctypes.byref(args), ctypes.c_void_p(stream)), lib)
     return dq, dk, dv, dadt, ddiag, dinit
+
+
+def _prelude_args(q, heads, tensors, num_angles, mimo_rotation) -> PreludeArgs:
+    batch, length, groups, rank, d_state = q.shape
+    args = PreludeArgs()
+    args.batch, args.length, args.groups, args.heads, args.rank = batch, length, groups, heads, rank
+    args.d_state, args.num_angles, args.mimo_rotation = d_state, num_angles, int(mimo_rotation)
+    args.device = q.device.index if q.device.index is not None else torch.cuda.current_device()
+    for name in _PRELUDE_TENSORS:
+        setattr(args, name, _desc(tensors.get(name)))
+    return args
+
+
+@torch.compiler.disable
+def ssd_prelude_forward(q, k, q_bias, k_bias, phase, scale, heads: int, mimo_rotation: bool):
+    """``m3_ssd_prelude_fwd``: float32 core operands ``(qf, kc)`` ``[B,L,H,R,N]`` from the raw
+    ``[B,L,G,R,N]`` q / k, biases, phase ``[B,L,H,S]`` (float32 or None) and scale ``[B,L,H]``."""
+    lib = load()
+    batch, length, _, rank, d_state = q.shape
+    qf = torch.empty(batch, length, heads, rank, d_state, device=q.device, dtype=torch.float32)
+    kc = torch.empty_like(qf)
+    args = _prelude_args(q, heads, dict(q=q, k=k, q_bias=q_bias, k_bias=k_bias, phase=phase, scale=scale, qf=qf,
+                                        kc=kc), 0 if phase is None else phase.shape[-1], mimo_rotation)
+    _check(lib.m3_ssd_prelude_fwd(ctypes.byref(args), ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)),
+           lib)
+    return qf, kc
+
+
+@torch.compiler.disable
+def ssd_prelude_backward(q, k, q_bias, k_bias, phase, scale, heads: int, mimo_rotation: bool, dqf, dkc,
+                         want_phase: bool):
+    """``m3_ssd_prelude_bwd``: ``(dqb, dkb, dphase or None, dscale)``, float32."""
+    lib = load()
+    dqb, dkb = torch.empty_like(dqf), torch.empty_like(dkc)
+    batch, length = q.shape[:2]
+    dphase = torch.empty_like(phase, dtype=torch.float32) if (want_phase and phase is not None) else None
+    dscale = torch.empty(batch, length, heads, device=q.device, dtype=torch.float32)
+    args = _prelude_args(q, heads, dict(q=q, k=k, q_bias=q_bias, k_bias=k_bias, phase=phase, scale=scale, dqf=dqf,
+                                        dkc=dkc, dqb=dqb, dkb=dkb, dphase=dphase, dscale=dscale),
+                         0 if phase is None else phase.shape[-1], mimo_rotation)
+    _check(lib.m3_ssd_prelude_bwd(ctypes.byref(args), ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)),
+           lib)
+    return dqb, dkb, dphase, dscale

@@ -740,3 +740,258 @@ int m3_ssd_train_fwd(const m3_ssd_args* args, void* stream) { return m3::ssd_lau
 int m3_ssd_train_bwd(const m3_ssd_args* args, void* stream) { return m3::ssd_launch(args, stream, true); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Training prelude: group expansion, bias, rotation and trapezoid scale of q / k
+// (mamba3/ops.py:35-84 rotate_qk, ops.py:665-676 / 719-745 bias and k * scale), fused into one
+// pass that writes the float32 core operands, and its backward. One warp per (batch, token, head);
+// lane l owns columns n = 4 l .. 4 l + 3 of every rank's row: a SISO rotation pair (2m, 2m + 1) is
+// lane-local, a MIMO pair (m, 2S + m) sits in lanes l and l + S / 2 (one shuffle).
+// The activation-dtype rounding of every step follows the reference's tensor ops.
+// ---------------------------------------------------------------------------------------------
+namespace m3 {
+namespace ssdt {
+
+template <typename T> struct PreludeLane {
+  const m3_prelude_args& a;
+  int b, t, h, g, lane, n0, S;
+  bool active, mimo;
+  __device__ PreludeLane(const m3_prelude_args& a_, int b_, int t_, int h_, int lane_)
+      : a(a_), b(b_), t(t_), h(h_), lane(lane_) {
+    g = h / (a.heads / a.groups);
+    n0 = 4 * lane;
+    active = n0 < a.d_state;
+    S = a.phase.data ? a.num_angles : 0;
+    mimo = a.mimo_rotation != 0;
+  }
+  // lane holding the rotation partner of this lane's columns (MIMO), else this lane
+  __device__ int partner() const {
+    if (!mimo || S == 0) return lane;
+    if (n0 < S) return lane + S / 2;  // columns n + 2S, same slot
+    if (n0 >= 2 * S && n0 < 3 * S) return lane - S / 2;
+    return lane;
+  }
+  // angle index of slot j (or -1: not rotated); first: this element is the pair's first member
+  __device__ int angle(int j, bool& first) const {
+    const int n = n0 + j;
+    first = true;
+    if (S == 0) return -1;
+    if (!mimo) {
+      first = (n & 1) == 0;
+      return (n >> 1) < S ? (n >> 1) : -1;
+    }
+    if (n < S) return n;
+    if (n >= 2 * S && n < 3 * S) {
+      first = false;
+      return n - 2 * S;
+    }
+    return -1;
+  }
+  __device__ float phase_at(int m) const {
+    const m3_tensor& p = a.phase;
+    return static_cast<const float*>(p.data)[b * p.stride[0] + (int64_t)t * p.stride[1] + h * p.stride[2] +
+                                             m * p.stride[3]];
+  }
+  // biased, unrotated q (which = 0) or k (1) of rank r, rounded to T
+  __device__ void biased(int which, int r, float (&x)[4]) const {
+    const m3_tensor& src = which ? a.k : a.q;
+    const m3_tensor& bias = which ? a.k_bias : a.q_bias;
+    const int64_t base = b * src.stride[0] + (int64_t)t * src.stride[1] + g * src.stride[2] + r * src.stride[3];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      x[j] = 0.0f;
+      if (active) {
+        x[j] = ld_t(src, base + (n0 + j) * src.stride[4]);
+        if (bias.data)
+          x[j] = rnd<T>(x[j] + rnd<T>(ld_t(bias, h * bias.stride[0] + r * bias.stride[1] + (n0 + j) * bias.stride[2])));
+      }
+    }
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(128) prelude_fwd_kernel(const m3_prelude_args a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (wid >= (int64_t)a.batch * a.length * a.heads) return;
+  const int h = (int)(wid % a.heads), t = (int)((wid / a.heads) % a.length), b = (int)(wid / ((int64_t)a.heads * a.length));
+  PreludeLane<T> pl(a, b, t, h, lane);
+  const int src = pl.partner();
+  float cs[4], sn[4];
+  int ang[4];
+  bool first[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    ang[j] = pl.active ? pl.angle(j, first[j]) : -1;
+    cs[j] = 1.0f, sn[j] = 0.0f;
+    if (ang[j] >= 0) {
+      float s_, c_;
+      sincosf(pl.phase_at(ang[j]), &s_, &c_);
+      cs[j] = rnd<T>(c_), sn[j] = rnd<T>(s_);
+    }
+  }
+  const float sc = rnd<T>(static_cast<const float*>(a.scale.data)[b * a.scale.stride[0] + (int64_t)t * a.scale.stride[1] +
+                                                                   h * a.scale.stride[2]]);
+  for (int which = 0; which < 2; ++which) {
+    for (int r = 0; r < a.rank; ++r) {
+      float x[4], o[4];
+      pl.biased(which, r, x);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        // partner element: same lane (SISO, slot j ^ 1) or the partner lane, slot j (MIMO)
+        const float other = pl.mimo ? __shfl_sync(0xffffffffu, x[j], src) : x[j ^ 1];
+        o[j] = x[j];
+        if (ang[j] >= 0) {
+          const float av = first[j] ? x[j] : other, bv = first[j] ? other : x[j];
+          o[j] = first[j] ? rnd<T>(rnd<T>(av * cs[j]) - rnd<T>(bv * sn[j]))
+                          : rnd<T>(rnd<T>(av * sn[j]) + rnd<T>(bv * cs[j]));
+        }
+        if (which) o[j] = rnd<T>(o[j] * sc);
+      }
+      if (pl.active) {
+        const m3_tensor& dst = which ? a.kc : a.qf;
+        *reinterpret_cast<float4*>(static_cast<float*>(dst.data) + b * dst.stride[0] + (int64_t)t * dst.stride[1] +
+                                   h * dst.stride[2] + r * dst.stride[3] + pl.n0) = make_float4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) prelude_bwd_kernel(const m3_prelude_args a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (wid >= (int64_t)a.batch * a.length * a.heads) return;
+  const int h = (int)(wid % a.heads), t = (int)((wid / a.heads) % a.length), b = (int)(wid / ((int64_t)a.heads * a.length));
+  PreludeLane<T> pl(a, b, t, h, lane);
+  const int src = pl.partner();
+  float cs[4], sn[4], ce[4], se[4], dph[4];
+  int ang[4];
+  bool first[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    ang[j] = pl.active ? pl.angle(j, first[j]) : -1;
+    cs[j] = ce[j] = 1.0f, sn[j] = se[j] = 0.0f, dph[j] = 0.0f;
+    if (ang[j] >= 0) {
+      sincosf(pl.phase_at(ang[j]), &se[j], &ce[j]);
+      cs[j] = rnd<T>(ce[j]), sn[j] = rnd<T>(se[j]);
+    }
+  }
+  const float sc = rnd<T>(static_cast<const float*>(a.scale.data)[b * a.scale.stride[0] + (int64_t)t * a.scale.stride[1] +
+                                                                   h * a.scale.stride[2]]);
+  float dsc = 0.0f;
+  for (int which = 0; which < 2; ++which) {
+    const m3_tensor& din = which ? a.dkc : a.dqf;
+    const m3_tensor& dout = which ? a.dkb : a.dqb;
+    for (int r = 0; r < a.rank; ++r) {
+      float x[4], d[4] = {0.f, 0.f, 0.f, 0.f};
+      pl.biased(which, r, x);
+      if (pl.active) {
+        const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(din.data) + b * din.stride[0] +
+                                                          (int64_t)t * din.stride[1] + h * din.stride[2] +
+                                                          r * din.stride[3] + pl.n0);
+        d[0] = v.x, d[1] = v.y, d[2] = v.z, d[3] = v.w;
+      }
+      float rot[4];
+      // forward rotated values (for the scale gradient) and the gradient before the scale
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float other = pl.mimo ? __shfl_sync(0xffffffffu, x[j], src) : x[j ^ 1];
+        rot[j] = x[j];
+        if (ang[j] >= 0) {
+          const float av = first[j] ? x[j] : other, bv = first[j] ? other : x[j];
+          rot[j] = first[j] ? rnd<T>(rnd<T>(av * cs[j]) - rnd<T>(bv * sn[j]))
+                            : rnd<T>(rnd<T>(av * sn[j]) + rnd<T>(bv * cs[j]));
+        }
+      }
+      if (which) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          dsc = fmaf(d[j], rot[j], dsc);
+          d[j] *= sc;
+        }
+      }
+      // rotation backward: out1 = a c - b s, out2 = a s + b c
+      float g[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float xo = pl.mimo ? __shfl_sync(0xffffffffu, x[j], src) : x[j ^ 1];
+        const float dother = pl.mimo ? __shfl_sync(0xffffffffu, d[j], src) : d[j ^ 1];
+        g[j] = d[j];
+        if (ang[j] >= 0) {
+          const float av = first[j] ? x[j] : xo, bv = first[j] ? xo : x[j];
+          const float d1 = first[j] ? d[j] : dother, d2 = first[j] ? dother : d[j];
+          g[j] = first[j] ? d1 * cs[j] + d2 * sn[j] : -d1 * sn[j] + d2 * cs[j];
+          if (first[j]) dph[j] += (d1 * av + d2 * bv) * (-se[j]) + (d2 * av - d1 * bv) * ce[j];
+        }
+      }
+      if (pl.active) {
+        *reinterpret_cast<float4*>(static_cast<float*>(dout.data) + b * dout.stride[0] + (int64_t)t * dout.stride[1] +
+                                   h * dout.stride[2] + r * dout.stride[3] + pl.n0) = make_float4(g[0], g[1], g[2], g[3]);
+      }
+    }
+  }
+  if (a.dphase.data) {
+    const m3_tensor& p = a.dphase;
+    float* dp = static_cast<float*>(p.data) + b * p.stride[0] + (int64_t)t * p.stride[1] + h * p.stride[2];
+    // every angle m < S has exactly one first member (column 2m SISO, m MIMO): its lane writes it
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (ang[j] >= 0 && first[j]) dp[ang[j] * p.stride[3]] = dph[j];
+  }
+  dsc = warp_sum(dsc);
+  if (lane == 0) {
+    const m3_tensor& s = a.dscale;
+    static_cast<float*>(s.data)[b * s.stride[0] + (int64_t)t * s.stride[1] + h * s.stride[2]] = dsc;
+  }
+}
+
+}  // namespace ssdt
+
+static int prelude_launch(const m3_prelude_args* args, void* stream, bool bwd) {
+  if (args == nullptr) return report_error(M3_ERR_ARGUMENT, "null argument struct");
+  const m3_prelude_args& a = *args;
+  if (a.batch <= 0 || a.length <= 0 || a.heads <= 0 || a.groups <= 0 || a.heads % a.groups != 0 || a.rank <= 0)
+    return report_error(M3_ERR_SHAPE, "batch, length, heads, groups and rank must be positive (heads divisible by groups)");
+  if (a.d_state <= 0 || a.d_state > 128 || a.d_state % 4 != 0)
+    return report_error(M3_ERR_SHAPE, "the prelude kernels serve d_state <= 128, a multiple of 4");
+  if (a.phase.data && (a.num_angles <= 0 || (a.mimo_rotation ? (a.num_angles % 4 != 0 || 4 * a.num_angles > a.d_state)
+                                                             : 2 * a.num_angles > a.d_state)))
+    return report_error(M3_ERR_SHAPE, "angle count does not fit the state width (MIMO: a multiple of 4)");
+  if (!a.q.data || !a.k.data || !a.scale.data || a.scale.dtype != M3_F32 || a.q.dtype != a.k.dtype)
+    return report_error(M3_ERR_ARGUMENT, "q, k (same dtype) and a float32 scale are required");
+  if ((a.q_bias.data == nullptr) != (a.k_bias.data == nullptr))
+    return report_error(M3_ERR_ARGUMENT, "q_bias and k_bias must be given together");
+  if (a.phase.data && a.phase.dtype != M3_F32) return report_error(M3_ERR_ARGUMENT, "phase must be float32");
+  const m3_tensor* rows[] = {bwd ? &a.dqf : &a.qf, bwd ? &a.dkc : &a.kc, bwd ? &a.dqb : &a.qf, bwd ? &a.dkb : &a.kc};
+  for (const m3_tensor* r : rows)
+    if (!r->data || r->dtype != M3_F32 || r->stride[4] != 1 || (reinterpret_cast<uintptr_t>(r->data) & 15u) ||
+        r->stride[0] % 4 || r->stride[1] % 4 || r->stride[2] % 4 || r->stride[3] % 4)
+      return report_error(M3_ERR_LAYOUT, "float32 [B,L,H,R,N] rows must be contiguous and 16-byte aligned");
+  if (bwd && (!a.dscale.data || a.dscale.dtype != M3_F32)) return report_error(M3_ERR_ARGUMENT, "dscale (float32) is required");
+  if (a.device >= 0 && cudaSetDevice(a.device) != cudaSuccess) return report_error(M3_ERR_CUDA, "cannot select the device");
+  const int64_t warps = (int64_t)a.batch * a.length * a.heads;
+  const unsigned grid = (unsigned)((warps + 3) / 4);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (a.q.dtype) {
+    case M3_BF16:
+      bwd ? ssdt::prelude_bwd_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(a)
+          : ssdt::prelude_fwd_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(a);
+      break;
+    case M3_F16:
+      bwd ? ssdt::prelude_bwd_kernel<__half><<<grid, 128, 0, st>>>(a) : ssdt::prelude_fwd_kernel<__half><<<grid, 128, 0, st>>>(a);
+      break;
+    default:
+      bwd ? ssdt::prelude_bwd_kernel<float><<<grid, 128, 0, st>>>(a) : ssdt::prelude_fwd_kernel<float><<<grid, 128, 0, st>>>(a);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return report_error(M3_ERR_CUDA, (std::string("prelude launch failed: ") + cudaGetErrorString(e)).c_str());
+  return M3_OK;
+}
+
+}  // namespace m3
+
+extern "C" {
+int m3_ssd_prelude_fwd(const m3_prelude_args* args, void* stream) { return m3::prelude_launch(args, stream, false); }
+int m3_ssd_prelude_bwd(const m3_prelude_args* args, void* stream) { return m3::prelude_launch(args, stream, true); }
+}

@@ -250,6 +250,48 @@ class _SSDCore(torch.autograd.Function):
         return dq, dk, dv, dadt, ddiag, dinit
 
 
+class _Prelude(torch.autograd.Function):
+    """Group expansion, bias, rotation and trapezoid scale of q / k on the prelude kernels
+    (``m3_ssd_prelude_fwd`` / ``_bwd``): ``(q, k, q_bias, k_bias, phase, scale) -> (qf, k*scale)``
+    as float32 ``[B,L,H,R,N]``."""
+
+    @staticmethod
+    def forward(ctx, q, k, q_bias, k_bias, phase, scale, heads, mimo_rotation):
+        phase32 = None if phase is None else phase.float()
+        qf, kc = _ext.ssd_prelude_forward(q, k, q_bias, k_bias, phase32, scale, heads, mimo_rotation)
+        ctx.save_for_backward(q, k, q_bias, k_bias, phase32, scale)
+        ctx.heads, ctx.mimo = heads, mimo_rotation
+        ctx.phase_dtype = None if phase is None else phase.dtype
+        return qf, kc
+
+    @staticmethod
+    def backward(ctx, dqf, dkc):
+        q, k, q_bias, k_bias, phase, scale = ctx.saved_tensors
+        shape = (*q.shape[:2], ctx.heads, *q.shape[3:])
+        dqf = q.new_zeros(shape, dtype=torch.float32) if dqf is None else dqf.float().contiguous()
+        dkc = torch.zeros_like(dqf) if dkc is None else dkc.float().contiguous()
+        dqb, dkb, dphase, dscale = _ext.ssd_prelude_backward(q, k, q_bias, k_bias, phase, scale, ctx.heads, ctx.mimo,
+                                                             dqf, dkc, want_phase=ctx.needs_input_grad[4])
+        batch, length, groups, rank, n = q.shape
+        per = ctx.heads // groups
+        dq = dqb.view(batch, length, groups, per, rank, n).sum(3).to(q.dtype) if ctx.needs_input_grad[0] else None
+        dk = dkb.view(batch, length, groups, per, rank, n).sum(3).to(k.dtype) if ctx.needs_input_grad[1] else None
+        dqbias = dqb.sum((0, 1)).to(q_bias.dtype) if (q_bias is not None and ctx.needs_input_grad[2]) else None
+        dkbias = dkb.sum((0, 1)).to(k_bias.dtype) if (k_bias is not None and ctx.needs_input_grad[3]) else None
+        if dphase is not None:
+            dphase = dphase.to(ctx.phase_dtype)
+        return dq, dk, dqbias, dkbias, dphase, dscale, None, None
+
+
+def _prelude_kernel_eligible(q, phase, mimo_rotation) -> bool:
+    """CUDA calls whose shapes the prelude kernels serve (d_state <= 128, a multiple of 4; MIMO
+    angle counts a multiple of 4)."""
+    n = q.shape[-1]
+    if not q.is_cuda or n > 128 or n % 4 or q.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        return False
+    return phase is None or not mimo_rotation or phase.shape[-1] % 4 == 0
+
+
 def _train_kernel_eligible(q, value) -> bool:
     """CUDA autograd calls whose shapes the training kernels serve (d_state <= 128, head_dim <= 64)."""
     return q.is_cuda and q.shape[-1] <= 128 and value.shape[-1] <= 64
@@ -263,15 +305,18 @@ def _scan_train(q, k, value, gate, adt, dt, trap_logits, D, *, mimo_x, mimo_z, m
     The core runs in float32 from the activation-dtype operands (no intermediate 16-bit rounding)."""
     heads = value.shape[2]
     act = value.dtype
-    qf = _expand_groups(q, heads)
-    kf = _expand_groups(k, heads)
-    if q_bias is not None:
-        qf = qf + q_bias.to(q.dtype)
-        kf = kf + k_bias.to(k.dtype)
-    if phase is not None:
-        qf, kf = rotate_qk(qf, kf, phase, mimo=mimo_rotation)
     sig, _, scale, diag = _scalar_prelude(adt, dt, trap_logits)
-    kc = kf * scale.to(k.dtype)[..., None, None]
+    if _prelude_kernel_eligible(q, phase, mimo_rotation):
+        qf, kc = _Prelude.apply(q, k, q_bias, k_bias, phase, scale, heads, mimo_rotation)
+    else:
+        qf = _expand_groups(q, heads)
+        kf = _expand_groups(k, heads)
+        if q_bias is not None:
+            qf = qf + q_bias.to(q.dtype)
+            kf = kf + k_bias.to(k.dtype)
+        if phase is not None:
+            qf, kf = rotate_qk(qf, kf, phase, mimo=mimo_rotation)
+        kc = kf * scale.to(k.dtype)[..., None, None]
 
     def rank_act(t, proj):  # [..., H, P] -> [..., H, R, P] in the activation dtype (ops.py:193-199)
         return t.unsqueeze(-2) if proj is None else t.unsqueeze(-2) * proj.to(t.dtype)
