@@ -380,7 +380,9 @@ def run_decode(world, rank, batch, drank, depth=DECODE["depth"], steps=64, prefi
     launches = 2 if step_kernel.startswith("two_pass") else 1
     out = {"us_per_step": us, "batch": batch, "steps": steps, "prefix": prefix,
            "model": f"Mamba3(2560, depth={depth}, mimo_rank={drank}) bf16, FP32 state, cuda_graph",
-           "gpu_launches": (launches + 1) * depth * steps + 1,
+           # per layer: the step kernels, the fused residual + RMSNorm, and (batch <= 4) the two
+           # projections on m3_gemv; plus the first norm of a step
+           "gpu_launches": (launches + 1 + (2 if batch <= 4 else 0)) * depth * steps + steps,
            "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                         "frac": gbs / pk["hbm_gbs"], "peak_kind": pk_kind,
                         "kernel": f"m3 step ({step_kernel})", "kernel_us": kus,

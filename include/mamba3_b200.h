@@ -158,6 +158,20 @@ typedef struct m3_norm_args {
 
 int m3_residual_rmsnorm(const m3_norm_args* args, void* stream);
 
+/*
+ * Few-row projection y = x W^T of a decode step (the in_proj / out_proj nn.Linear calls of
+ * mamba3/model.py:422-484 at batch <= 4, a library GEMM in the reference): x [rows][in_dim],
+ * W [out_dim][in_dim], y [rows][out_dim], one 16-bit dtype; FP32 accumulation, y rounded once.
+ * rows 1..4, in_dim a multiple of 8 (<= 16384); x / W rows contiguous and 16-byte aligned.
+ */
+typedef struct m3_gemv_args {
+  int64_t out_dim, in_dim;
+  int32_t rows, device; /* device: CUDA ordinal of the tensors and `stream` (-1: current) */
+  m3_tensor x, w, y;
+} m3_gemv_args;
+
+int m3_gemv(const m3_gemv_args* args, void* stream);
+
 /* Chunked SSD forward. Returns M3_OK or an M3_ERR_* code. */
 int m3_scan_fwd(const m3_scan_args* args, void* stream);
 

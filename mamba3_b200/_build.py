@@ -24,7 +24,7 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC",
     "--expt-relaxed-constexpr",
 ]
-UNITS = ["capi.cu", "step.cu", "scan_simt.cu", "scan_umma.cu", "noalloc.cu", "norm.cu", "ssd_train.cu"]
+UNITS = ["capi.cu", "step.cu", "scan_simt.cu", "scan_umma.cu", "noalloc.cu", "norm.cu", "ssd_train.cu", "gemv.cu"]
 
 
 def sources() -> list[Path]:

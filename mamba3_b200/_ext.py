@@ -59,6 +59,11 @@ class ScanArgs(ctypes.Structure):
         (name, M3Tensor) for name in _SCAN_TENSORS]
 
 
+class GemvArgs(ctypes.Structure):
+    _fields_ = [("out_dim", ctypes.c_int64), ("in_dim", ctypes.c_int64), ("rows", ctypes.c_int32),
+                ("device", ctypes.c_int32)] + [(name, M3Tensor) for name in ("x", "w", "y")]
+
+
 class NormArgs(ctypes.Structure):
     _fields_ = [("rows", ctypes.c_int64), ("dim", ctypes.c_int32), ("device", ctypes.c_int32),
                 ("eps", ctypes.c_float), ("reserved", ctypes.c_int32)] + [
@@ -131,6 +136,8 @@ def load() -> ctypes.CDLL:
         lib.m3_scan_workspace_bytes.restype = ctypes.c_int64
         lib.m3_step_workspace_bytes.argtypes = [ctypes.POINTER(StepArgs)]
         lib.m3_step_workspace_bytes.restype = ctypes.c_int64
+        lib.m3_gemv.argtypes = [ctypes.POINTER(GemvArgs), ctypes.c_void_p]
+        lib.m3_gemv.restype = ctypes.c_int
         lib.m3_residual_rmsnorm.argtypes = [ctypes.POINTER(NormArgs), ctypes.c_void_p]
         lib.m3_residual_rmsnorm.restype = ctypes.c_int
         lib.m3_last_scan_kernel.argtypes = []
@@ -453,3 +460,29 @@ def ssd_prelude_backward(q, k, q_bias, k_bias, phase, scale, heads: int, mimo_ro
     _check(lib.m3_ssd_prelude_bwd(ctypes.byref(args), ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)),
            lib)
     return dqb, dkb, dphase, dscale
+
+
+def gemv_eligible(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """Few-row projections ``m3_gemv`` serves: 1..4 rows, one 16-bit dtype, contiguous aligned rows."""
+    if not (x.is_cuda and w.is_cuda) or x.dtype != w.dtype or x.dtype not in (torch.bfloat16, torch.float16):
+        return False
+    rows = x.numel() // max(x.shape[-1], 1)
+    i = x.shape[-1]
+    return (1 <= rows <= 4 and i % 8 == 0 and i <= 16384 and w.dim() == 2 and w.shape[1] == i and w.stride(1) == 1
+            and w.stride(0) % 8 == 0 and w.data_ptr() % 16 == 0)
+
+
+@torch.compiler.disable
+def gemv(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x @ w.T`` on ``m3_gemv`` for a few rows of x (decode-step projections)."""
+    lib = load()
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    y = torch.empty(x2.shape[0], w.shape[0], device=x.device, dtype=x.dtype)
+    args = GemvArgs()
+    args.out_dim, args.in_dim, args.rows = w.shape[0], w.shape[1], x2.shape[0]
+    args.device = x.device.index if x.device.index is not None else torch.cuda.current_device()
+    args.x, args.w, args.y = _desc(x2), _desc(w), _desc(y)
+    _check(lib.m3_gemv(ctypes.byref(args), ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)), lib)
+    return y.view(*x.shape[:-1], w.shape[0])

@@ -91,6 +91,65 @@ __global__ void __launch_bounds__(kNormThreads) residual_rmsnorm_rowblock(const 
   }
 }
 
+// Few rows of one 16-bit dtype T throughout (x, m, out_x, out_n, w: a bf16 / fp16 model's decode
+// step): one CTA per row, each thread holding up to kRowChunks 16-byte chunks of the row in
+// registers; every load is issued before the block reduction, the row is read once.
+constexpr int kRowChunks = 4;  // dim <= 4 * 8 * 256 = 8192
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) residual_rmsnorm_row16(const m3_norm_args a) {
+  __shared__ float part[kNormThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int D = a.dim, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const T* xp = static_cast<const T*>(a.x.data) + row * a.x.stride[0];
+  const T* mp = a.m.data ? static_cast<const T*>(a.m.data) + row * a.m.stride[0] : nullptr;
+  const T* wp = static_cast<const T*>(a.w.data);
+  float r[kRowChunks][8];
+  uint4 wv[kRowChunks];
+  float ss = 0.0f;
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int i = 8 * (tid + kNormThreads * c);
+    uint4 xv = make_uint4(0u, 0u, 0u, 0u), mv = xv;
+    wv[c] = xv;
+    if (i < D) {
+      xv = *reinterpret_cast<const uint4*>(xp + i);
+      if (mp) mv = *reinterpret_cast<const uint4*>(mp + i);
+      wv[c] = *reinterpret_cast<const uint4*>(wp + i);
+    }
+    const T* xe = reinterpret_cast<const T*>(&xv);
+    const T* me = reinterpret_cast<const T*>(&mv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      // the residual stream holds the rounded sum (the reference adds in this dtype)
+      r[c][e] = mp ? rnd<T>(to_f(xe[e]) + to_f(me[e])) : to_f(xe[e]);
+      ss += r[c][e] * r[c][e];
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) part[warp] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) tot += part[w];
+  const float inv = rsqrtf(tot / D + a.eps);
+  T* op = a.out_x.data ? static_cast<T*>(a.out_x.data) + row * a.out_x.stride[0] : nullptr;
+  T* np = static_cast<T*>(a.out_n.data) + row * a.out_n.stride[0];
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int i = 8 * (tid + kNormThreads * c);
+    if (i >= D) continue;
+    T xo[8], no[8];
+    const T* we = reinterpret_cast<const T*>(&wv[c]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      xo[e] = from_f<T>(r[c][e]);
+      no[e] = from_f<T>(r[c][e] * inv * to_f(we[e]));
+    }
+    if (op) *reinterpret_cast<uint4*>(op + i) = *reinterpret_cast<const uint4*>(xo);
+    *reinterpret_cast<uint4*>(np + i) = *reinterpret_cast<const uint4*>(no);
+  }
+}
+
 // Vector path: fp32 residual, dim % 128 == 0, contiguous 16-byte aligned rows; m and out_n 16-bit
 // (TM / TN) or fp32. Each lane owns float4 groups lane, lane + 32, ... (NV of them, up to 16).
 template <typename TM, typename TN, int NV>
@@ -196,7 +255,15 @@ extern "C" int m3_residual_rmsnorm(const m3_norm_args* args, void* stream) {
                                   (a.m.stride[0] * msz) % (4 * msz) == 0)) &&
                    (!a.out_x.data || rowvec(a.out_x, 4));
   cudaError_t e;
-  if (a.rows < 8 * 148) {  // too few rows for a warp each to fill the GPU
+  const bool one16 = a.x.dtype != M3_F32 && a.w.dtype == a.x.dtype && a.out_n.dtype == a.x.dtype &&
+                     (!a.m.data || a.m.dtype == a.x.dtype) && a.dim % 8 == 0 && a.dim <= 8 * kNormThreads * kRowChunks &&
+                     a.w.stride[0] == 1 && aligned16(a.w.data) && rowvec(a.x, 2) && rowvec(a.out_n, 2) &&
+                     (!a.m.data || rowvec(a.m, 2)) && (!a.out_x.data || rowvec(a.out_x, 2));
+  if (a.rows < 8 * 148 && one16) {  // a 16-bit model's decode step
+    if (a.x.dtype == M3_BF16) residual_rmsnorm_row16<__nv_bfloat16><<<(unsigned)a.rows, kNormThreads, 0, st>>>(a);
+    else residual_rmsnorm_row16<__half><<<(unsigned)a.rows, kNormThreads, 0, st>>>(a);
+    e = cudaGetLastError();
+  } else if (a.rows < 8 * 148) {  // too few rows for a warp each to fill the GPU
     residual_rmsnorm_rowblock<<<(unsigned)a.rows, kNormThreads, 0, st>>>(a);
     e = cudaGetLastError();
   } else if (vec) {

@@ -126,6 +126,8 @@ class _Mamba3Mixer(nn.Module):
         layer = getattr(self, name)
         weight = layer.weight
         if not (hidden.is_cuda and torch.is_autocast_enabled("cuda") and weight.dtype == torch.float32):
+            if self._few_row_projection(hidden, weight):
+                return _ext.gemv(hidden, weight)
             return layer(hidden)
         dtype = torch.get_autocast_dtype("cuda")
         key = (name, dtype)
@@ -134,7 +136,17 @@ class _Mamba3Mixer(nn.Module):
         if entry is None or entry[:2] != stamp:
             entry = (*stamp, weight.detach().to(dtype))
             self._weight_casts[key] = entry
-        return F.linear(hidden.to(dtype), entry[2])
+        hidden = hidden.to(dtype)
+        if self._few_row_projection(hidden, entry[2]):
+            return _ext.gemv(hidden, entry[2])
+        return F.linear(hidden, entry[2])
+
+    @staticmethod
+    def _few_row_projection(hidden: torch.Tensor, weight: torch.Tensor) -> bool:
+        """Decode-step projections (at most 4 rows, inference) run as a weight stream on m3_gemv."""
+        if torch.is_grad_enabled() and (hidden.requires_grad or weight.requires_grad):
+            return False
+        return _ext.gemv_eligible(hidden, weight)
 
     def _views(self, projected: torch.Tensor):
         batch, length, _ = projected.shape
@@ -542,11 +554,32 @@ class Mamba3(nn.Module):
             if len(cache) != len(self.layers):
                 raise ValueError(f"expected cache for {len(self.layers)} layers")
             layer_caches = list(cache)
+        if self._fused_stream(x):
+            return self._step_fused(x, layer_caches)
         new_cache = []
         for layer, layer_cache in zip(self.layers, layer_caches):
             x, updated = layer.step(x, layer_cache)
             new_cache.append(updated)
         return self.norm_f(x), new_cache
+
+    def _step_fused(self, x: torch.Tensor, layer_caches):
+        """One decode step with the residual stream between blocks on m3_residual_rmsnorm (the
+        same arithmetic as `hidden + mixer.step(norm(hidden))` per block and `norm_f` at the end)."""
+        act = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else x.dtype
+        first = self.layers[0].norm
+        normed = _ext.residual_rmsnorm(x, None, first.weight, first.eps, out_dtype=act)
+        resid, new_cache = x, []
+        for i, (layer, layer_cache) in enumerate(zip(self.layers, layer_caches)):
+            mixed, updated = layer.mixer.step(normed, layer_cache)
+            new_cache.append(updated)
+            if i + 1 == len(self.layers):
+                return _ext.residual_rmsnorm(resid, mixed, self.norm_f.weight, self.norm_f.eps, out_dtype=x.dtype), new_cache
+            nxt = self.layers[i + 1].norm
+            if resid is x:  # never write into the caller's input
+                resid = torch.empty_like(x)
+                normed = _ext.residual_rmsnorm(x, mixed, nxt.weight, nxt.eps, out_dtype=act, out_x=resid)
+            else:
+                normed = _ext.residual_rmsnorm(resid, mixed, nxt.weight, nxt.eps, out_dtype=act, out_x=resid)
 
     def set_chunk_sizes(self, *, training: int | None = None, inference: int | None = None) -> Mamba3:
         """Override scan chunk sizes without rebuilding the model (mamba3/model.py:632-654)."""

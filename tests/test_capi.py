@@ -95,3 +95,15 @@ def test_workspace_query_rejects_non_positive_sizes_without_a_device():
     args.device = 0
     rc = lib.m3_scan_fwd_noalloc(ctypes.byref(args), None)
     assert rc in (1, 5)  # M3_ERR_SHAPE, or M3_ERR_CUDA where no device can be selected
+
+
+def test_gemv_rejects_bad_arguments_without_a_device():
+    lib = _ext.load()
+    assert lib.m3_gemv(None, None) == 4
+    args = _ext.GemvArgs()
+    args.out_dim, args.in_dim, args.rows, args.device = 16, 12, 1, -1
+    assert lib.m3_gemv(ctypes.byref(args), None) == 1  # in_dim not a multiple of 8
+    args.in_dim, args.rows = 16, 5
+    assert lib.m3_gemv(ctypes.byref(args), None) == 1  # more than 4 rows
+    args.rows = 1
+    assert lib.m3_gemv(ctypes.byref(args), None) != 0  # tensors missing
