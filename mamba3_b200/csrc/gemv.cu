@@ -32,6 +32,21 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const m3_gemv_args a
   T* xs = reinterpret_cast<T*>(gsm);  // [M][I]
   const int I = (int)a.in_dim;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // Launched as a programmatic dependent of the kernel before it in a decode step: release the next
+  // kernel, pull this warp's weight rows (never written by any kernel) towards L2 while the
+  // previous kernel finishes, then wait for it before touching x or y.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  {
+    const int64_t op = ((int64_t)blockIdx.x * (kGemvThreads / 32) + warp) * kRowsPerWarp;
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r)
+      if (op + r < a.out_dim) {
+        const T* row = static_cast<const T*>(a.w.data) + (op + r) * a.w.stride[0];
+        for (int i = 64 * lane; i < I; i += 64 * 32)  // one 128-byte line per lane and step
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(row + i));
+      }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const T* xp = static_cast<const T*>(a.x.data);
   for (int c = threadIdx.x; c < M * (I / 8); c += kGemvThreads) {
     const int m = c / (I / 8), i = 8 * (c % (I / 8));
@@ -90,8 +105,17 @@ template <typename T, int M> cudaError_t launch_m(const m3_gemv_args& a, cudaStr
   cudaError_t e = cudaFuncSetAttribute(gemv_kernel<T, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int64_t per_cta = (kGemvThreads / 32) * kRowsPerWarp;
-  gemv_kernel<T, M><<<(unsigned)((a.out_dim + per_cta - 1) / per_cta), kGemvThreads, smem, stream>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((a.out_dim + per_cta - 1) / per_cta));
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<T, M>, a);
 }
 
 template <typename T> cudaError_t launch_t(const m3_gemv_args& a, cudaStream_t stream) {

@@ -98,6 +98,10 @@ constexpr int kRowChunks = 4;  // dim <= 4 * 8 * 256 = 8192
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads) residual_rmsnorm_row16(const m3_norm_args a) {
   __shared__ float part[kNormThreads / 32];
+  // programmatic dependent of the projection before it: release the next kernel, wait for the
+  // previous one before reading anything
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t row = blockIdx.x;
   const int D = a.dim, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const T* xp = static_cast<const T*>(a.x.data) + row * a.x.stride[0];
@@ -260,9 +264,17 @@ extern "C" int m3_residual_rmsnorm(const m3_norm_args* args, void* stream) {
                      a.w.stride[0] == 1 && aligned16(a.w.data) && rowvec(a.x, 2) && rowvec(a.out_n, 2) &&
                      (!a.m.data || rowvec(a.m, 2)) && (!a.out_x.data || rowvec(a.out_x, 2));
   if (a.rows < 8 * 148 && one16) {  // a 16-bit model's decode step
-    if (a.x.dtype == M3_BF16) residual_rmsnorm_row16<__nv_bfloat16><<<(unsigned)a.rows, kNormThreads, 0, st>>>(a);
-    else residual_rmsnorm_row16<__half><<<(unsigned)a.rows, kNormThreads, 0, st>>>(a);
-    e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)a.rows);
+    cfg.blockDim = dim3(kNormThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    e = a.x.dtype == M3_BF16 ? cudaLaunchKernelEx(&cfg, residual_rmsnorm_row16<__nv_bfloat16>, a)
+                             : cudaLaunchKernelEx(&cfg, residual_rmsnorm_row16<__half>, a);
   } else if (a.rows < 8 * 148) {  // too few rows for a warp each to fill the GPU
     residual_rmsnorm_rowblock<<<(unsigned)a.rows, kNormThreads, 0, st>>>(a);
     e = cudaGetLastError();

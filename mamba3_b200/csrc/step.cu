@@ -205,6 +205,18 @@ __global__ void __launch_bounds__(kStepThreads) step_kernel(const m3_step_args a
   const int h = blockIdx.y, b = blockIdx.z;
   const int p0 = blockIdx.x * rows_per_cta;
   const int N = a.d_state, P = a.head_dim;
+  // Launched as a programmatic dependent of the projection before it: release the next kernel, pull
+  // this CTA's state rows towards L2 (a prefetch has no effect on the values read), then wait for
+  // the previous kernel before reading any input.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (a.state.stride[3] == 1) {
+    const float* sp = static_cast<const float*>(a.state.data) + b * a.state.stride[0] + h * a.state.stride[1];
+    for (int i = threadIdx.x; i < rows_per_cta * ((N + 31) / 32); i += blockDim.x) {
+      const int p = p0 + i / ((N + 31) / 32), n = 32 * (i % ((N + 31) / 32));
+      if (p < P) asm volatile("prefetch.global.L2 [%0];" ::"l"(sp + p * a.state.stride[2] + n));
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   extern __shared__ float sm[];
   const float* s_q = sm + 128;
@@ -1101,8 +1113,17 @@ static cudaError_t launch_step_r(const m3_step_args& a, cudaStream_t stream) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
     }
-    kern<<<grid, kStepThreads, smem, stream>>>(a, rows);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kStepThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a, rows);
   };
   if (N <= 32) return go(step_kernel<T, R, 1>);
   if (N <= 64) return go(step_kernel<T, R, 2>);
