@@ -241,6 +241,39 @@ def test_two_pass_decode_kernels_against_oracle(rank, dtype):
 
 
 @pytest.mark.parametrize("rank", [1, 4])
+@pytest.mark.parametrize("batch", [1, 3])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_small_batch_graph_decoder_against_oracle(rank, batch, dtype):
+    """The small-batch decode path under the CUDA-graph decoder: projections on the few-row GEMV,
+    block boundaries on the fused residual + RMSNorm kernel, the chain of dependent launches, the
+    single-pass step kernel; against the oracle on the same 16-bit parameters and inputs."""
+    torch.manual_seed(1)
+    model = Mamba3(512, d_state=128, depth=2, mimo_rank=rank).cuda().to(dtype).eval()
+    cfg = _cfg(model)
+    sd = {key: val.detach().float().cpu().numpy() for key, val in model.state_dict().items()}
+    prefix, steps = 24, 4
+    x = torch.randn(batch, prefix + steps, 512, device="cuda", dtype=dtype)
+    decoder = model.cuda_graph(batch_size=batch)
+    with torch.inference_mode():
+        _, cache = model.prefill(x[:, :prefix])
+        for mine, theirs in zip(decoder.cache, cache):
+            for dst, src in zip(mine, theirs):
+                dst.copy_(src)
+        outs = [decoder(x[:, t:t + 1]).clone() for t in range(prefix, prefix + steps)]
+    torch.cuda.synchronize()
+    assert _ext.last_step_kernel() == "single"
+    xn = _np(x)
+    _, caches = O.model_prefill(cfg, sd, xn[:, :prefix])
+    expected = []
+    for t in range(prefix, prefix + steps):
+        o, caches = O.model_step(cfg, sd, xn[:, t:t + 1], caches)
+        expected.append(o)
+    assert rel_err(torch.cat(outs, 1).float(), np.concatenate(expected, 1)) < 2e-2
+    for layer in range(2):
+        assert rel_err(decoder.cache[layer][1], caches[layer][1]) < STATE_TOL[dtype]
+
+
+@pytest.mark.parametrize("rank", [1, 4])
 def test_bf16_graph_decoder_at_batch_64_against_oracle(rank):
     """The decode benchmark's path: Mamba3(2560) bf16 parameters, CUDA-graph decoder at batch 64
     (two-pass kernels, state updated in place), after a kernel prefill; against the oracle run on
