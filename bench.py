@@ -571,9 +571,9 @@ def reference_gpu_decode(batch, our_us_per_layer, steps=64):
 
 
 def cpu_config1() -> dict:
-    """BASELINE config 1 in full on the host cores with the reference's portable PyTorch path:
-    Mamba3(256, depth=4), fp32, manual_seed(0), x ~ N(0,1) [2, 1024, 256]: forward, then prefill of
-    the same x and 64 step() calls with fresh N(0,1) [2, 1, 256] inputs."""
+    """The CPU-reference configuration in full on the host cores with the reference's portable
+    PyTorch path: Mamba3(256, depth=4), fp32, manual_seed(0), x ~ N(0,1) [2, 1024, 256]: forward,
+    then prefill of the same x and 64 step() calls with fresh N(0,1) [2, 1, 256] inputs."""
     try:
         ref = import_reference()
     except RuntimeError as exc:
@@ -600,7 +600,8 @@ def cpu_config1() -> dict:
 
 
 def gpu_config1() -> dict:
-    """The same config 1 through this package on the GPU (fp32: the CUDA-core scan kernel)."""
+    """The same CPU-reference configuration through this package on the GPU (fp32: the CUDA-core
+    scan kernel)."""
     from mamba3_b200 import Mamba3
     torch.manual_seed(0)
     model = Mamba3(256, d_state=128, depth=4, mimo_rank=1).eval().cuda()

@@ -17,7 +17,7 @@ Cases (reference tests they mirror: tests/test_scan.py:285-312, 385-435; tests/t
   * the in-kernel blocked phase carried across 2,048 blocks (L = 131,072), rank 1 and rank 4;
   * the two-pass decode kernels at B*H >= 296 in bf16 / fp16, rank 1 and rank 4 (rank 4 takes the
     16-byte-row prep and the reduce-scatter stream pass), in model mode as the decoder runs them;
-  * BASELINE config 1 in full: fp32 Mamba3(256, depth=4), [2, 1024, 256], forward -> prefill ->
+  * the CPU-reference configuration in full: fp32 Mamba3(256, depth=4), [2, 1024, 256], forward -> prefill ->
     64 steps.
 """
 
@@ -306,7 +306,7 @@ def test_bf16_graph_decoder_at_batch_64_against_oracle(rank):
 
 
 # ---------------------------------------------------------------------------------------------
-# BASELINE config 1 in full
+# The CPU-reference configuration in full
 # ---------------------------------------------------------------------------------------------
 
 def test_config1_forward_prefill_and_64_steps_fp32():
